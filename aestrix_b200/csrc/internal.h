@@ -1,0 +1,60 @@
+// internal.h — host-side internals shared by the translation units of
+// libaestrix_cuda: the context object, error reporting and TMA tensor-map
+// construction.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/aestrix_cuda.h"
+
+struct aex_ctx {
+  int device = 0;
+  int sm_count = 0;
+  int* d_status = nullptr;  // device status word written by kernels on a bounded-wait expiry
+  void* scratch = nullptr;  // grown on demand by entry points that need workspace
+  size_t scratch_bytes = 0;
+  std::string last_error;
+};
+
+struct aex_qweight {
+  int n = 0, k = 0, group_size = 64;
+  int n_tiles = 0;             // ceil(n / kQTileN)
+  uint8_t* packed = nullptr;   // tile layout, see qmm_sm100.cu
+  float* scale = nullptr;      // [n_tiles*kQTileN, k/64] f32 (zero for padded rows)
+  float* bias = nullptr;       // same shape
+  size_t packed_bytes = 0;
+};
+
+namespace aex {
+
+int set_error(aex_ctx* ctx, int code, const char* fmt, ...);
+int cuda_error(aex_ctx* ctx, cudaError_t e, const char* what);
+
+#define AEX_CUDA_TRY(ctx, expr)                                   \
+  do {                                                            \
+    cudaError_t _e = (expr);                                      \
+    if (_e != cudaSuccess) return ::aex::cuda_error(ctx, _e, #expr); \
+  } while (0)
+
+// Ensure the context's device is current on this thread.
+int bind_device(aex_ctx* ctx);
+
+// Grow-only context scratch.
+int ensure_scratch(aex_ctx* ctx, size_t bytes, void** out);
+
+// Encode a tiled TMA descriptor for a bf16 (or other 2-byte) tensor.
+// dims[0] is the contiguous dimension; strides_bytes has rank-1 entries
+// (strides of dims 1..rank-1). Returns AEX_OK or AEX_ERR_INVALID_ARG/CUDA.
+int make_tmap(aex_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dtype, const void* base, int rank,
+              const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+              CUtensorMapSwizzle swizzle);
+
+// Check the last kernel launch.
+int check_launch(aex_ctx* ctx, const char* what);
+
+}  // namespace aex

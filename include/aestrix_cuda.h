@@ -1,0 +1,192 @@
+/*
+ * aestrix_cuda.h — C ABI of libaestrix_cuda, the B200 (sm_100a) implementation of
+ * the FLUX.2-klein DiT joint attention and the MLX-layout 4-bit affine linears
+ * that feed it.
+ *
+ * Conventions
+ *  - Every entry point returns an int status (AEX_OK == 0). On failure the
+ *    context's message is available from aex_last_error_string(ctx). No entry
+ *    point aborts, traps or exits the process.
+ *  - Device pointers are plain `void*`/typed pointers into CUDA global memory of
+ *    the context's device. `aex_stream` is a cudaStream_t (NULL = legacy
+ *    default stream). All compute entry points are asynchronous on that stream.
+ *  - bf16 data is passed as uint16_t bit patterns (or void*), f32 as float.
+ *  - One aex_ctx per device per host thread; distinct contexts may be used
+ *    concurrently, a single context may not.
+ *  - Kernels never spin without bound: a device-side wait that expires records
+ *    a code that aex_sync / aex_device_status report as AEX_ERR_DEVICE.
+ *
+ * Each declaration cites the reference (PowerBeef/Aestrix, "Imarello") interface
+ * it replaces as path:line within that project.
+ */
+#ifndef AESTRIX_CUDA_H
+#define AESTRIX_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AEX_ABI_VERSION 1
+
+/* Status codes. Reference: Swift `throws` of DirectQmmSpike.SpikeError
+ * (Sources/ImarelloDirect/DirectQmmSpike.swift:17-27) and the command-buffer
+ * error check (Sources/ImarelloDirect/DirectDiTStep.swift:968-970). */
+#define AEX_OK 0
+#define AEX_ERR_INVALID_ARG 1 /* bad shape, stride, alignment or NULL pointer; nothing launched */
+#define AEX_ERR_UNSUPPORTED 2 /* valid but not implemented (e.g. head_dim != 128) */
+#define AEX_ERR_CUDA 3        /* a CUDA runtime/driver call failed */
+#define AEX_ERR_NCCL 4        /* an NCCL call failed */
+#define AEX_ERR_TIMEOUT 5     /* aex_sync gave up waiting */
+#define AEX_ERR_OOM 6         /* device allocation failed */
+#define AEX_ERR_DEVICE 7      /* a kernel reported a device-side status (bounded wait expired) */
+
+typedef struct aex_ctx aex_ctx;
+typedef struct aex_qweight aex_qweight;
+typedef void* aex_stream; /* cudaStream_t */
+
+/* ------------------------------------------------------------------ context */
+
+int aex_abi_version(void);
+
+/* Create a context bound to CUDA device `device`. Reference: the engine
+ * constructors that own a device and queue, DirectDiTStep.init
+ * (Sources/ImarelloDirect/DirectDiTStep.swift:74-132). */
+int aex_ctx_create(int device, aex_ctx** out);
+void aex_ctx_destroy(aex_ctx* ctx);
+
+/* Last error message of this context ("" if none). Valid until the next call
+ * on the same context. NULL ctx returns the message of the last failed
+ * aex_ctx_create on this thread. */
+const char* aex_last_error_string(const aex_ctx* ctx);
+
+/* Wait for `stream` with a bound. timeout_ms <= 0 waits without a bound on the
+ * host side (kernels themselves still never spin forever). Returns
+ * AEX_ERR_TIMEOUT if the stream is still busy at the deadline, AEX_ERR_DEVICE
+ * if a kernel recorded a device-side status. Reference: the blocking
+ * `waitUntilCompleted` + error check at DirectDiTStep.swift:968-970. */
+int aex_sync(aex_ctx* ctx, aex_stream stream, int timeout_ms);
+
+/* Read (and clear) the device status word the kernels write on a bounded-wait
+ * expiry. *code receives 0 when no kernel reported anything. Synchronizes the
+ * device. */
+int aex_device_status(aex_ctx* ctx, int* code);
+
+/* Number of SMs of the context's device. */
+int aex_device_sm_count(const aex_ctx* ctx);
+
+/* -------------------------------------------------------------- attention */
+
+/* Strided 4-D view [batch, seq, head, dim] of a bf16 tensor; the dim stride is
+ * 1. [B,H,S,D] tensors of the MLX path use (H*S*D, D, S*D); the direct
+ * engine's [J, 24, 128] rows use (J*3072, 3072, 128). All strides in elements,
+ * each a multiple of 8 (16 bytes), base pointer 16-byte aligned. */
+typedef struct aex_bshd {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_s;
+  int64_t stride_h;
+} aex_bshd;
+
+typedef struct aex_attention_args {
+  aex_bshd q, k, v; /* bf16 inputs (pre-norm, pre-RoPE when the norm/rope fields are set) */
+  aex_bshd out;     /* bf16 output; may alias nothing else */
+  int batch;
+  int seq;          /* joint length J = text rows then image rows */
+  int heads;
+  int head_dim;     /* must be 128 */
+  /* QK-RMSNorm: y = x * rsqrt(mean(x^2) + eps) * w, f32 math, per head over
+   * head_dim. NULL weights skip the norm for that operand. */
+  const float* norm_q_weight; /* [head_dim] f32 or NULL */
+  const float* norm_k_weight; /* [head_dim] f32 or NULL */
+  float eps;
+  /* Interleaved-pair rotary embedding with per-row tables [seq, head_dim/2]
+   * f32 (row r of the tables rotates token r). NULL skips RoPE. */
+  const float* rope_cos;
+  const float* rope_sin;
+  float scale; /* softmax scale; <= 0 selects 1/sqrt(head_dim) */
+} aex_attention_args;
+
+/* Fused QK-RMSNorm -> 2-D axial RoPE -> non-causal softmax(scale*QK^T)V.
+ * Replaces the composition AttentionUtils.processQKV's norm step
+ * (Sources/ImarelloDiT/AttentionUtils.swift:37-50), applyRopeBSHD
+ * (AttentionUtils.swift:263-298) and computeAttention ->
+ * MetalFlashAttention.scaledDotProductAttention (AttentionUtils.swift:65-135,
+ * Sources/ImarelloDiT/MetalFlashAttention.swift:44-78); and in the direct
+ * engine rms + rope + attention (Sources/ImarelloDirect/DirectDiTStep.swift:
+ * 408-488, 568-571, 612-615). With both norm weights and the rope tables NULL
+ * it is exactly scaledDotProductAttention(query:key:value:scale:mask: nil).
+ * Uses context-owned scratch for the normalized Q/K (grown on demand). */
+int aex_joint_attention(aex_ctx* ctx, const aex_attention_args* args, aex_stream stream);
+
+/* Bytes of scratch aex_joint_attention needs for these args (0 when no norm
+ * and no RoPE are requested). */
+size_t aex_joint_attention_scratch_bytes(const aex_attention_args* args);
+
+/* Same computation with caller-provided scratch of at least
+ * aex_joint_attention_scratch_bytes(args) bytes (256-byte aligned). */
+int aex_joint_attention_ws(aex_ctx* ctx, const aex_attention_args* args, void* scratch, size_t scratch_bytes,
+                           aex_stream stream);
+
+/* 4-axis rotary tables. ids: [n, 4] f32 positions (t, h, w, l); out cos/sin:
+ * [n, sum(axes_dim)/2] f32 (device pointers). Reference: Flux2PosEmbed
+ * (Sources/ImarelloDiT/PosEmbed.swift:12-47), Flux2RoPE.frequencies
+ * (Sources/ImarelloCore/Flux2RoPE.swift:16-63). */
+int aex_rope_tables(aex_ctx* ctx, const float* ids, int n, float theta, const int* axes_dim, int n_axes,
+                    float* cos_out, float* sin_out, aex_stream stream);
+
+/* ------------------------------------------------------ 4-bit affine linear */
+
+/* Dequantize an MLX affine-quantized matrix straight from its on-disk layout:
+ * packed uint32 [n, k/8] (LSB-first nibbles), scales/biases bf16 [n, k/group],
+ * out bf16 [n, k] = bf16_rne(f32(scale*q + bias)). Device pointers.
+ * Reference: the CPU dequant DirectTEEncoder.embedRow
+ * (Sources/ImarelloDirect/DirectTEEncoder.swift:104-123) and MLX `dequantized`
+ * (DirectTEEncoder.swift:129-134). group_size must be 64, bits 4. */
+int aex_dequantize_mlx(aex_ctx* ctx, const uint32_t* packed, const uint16_t* scales, const uint16_t* biases,
+                       int n, int k, int group_size, int bits, uint16_t* out, aex_stream stream);
+
+/* Unpack an MLX affine 4-bit weight (device pointers in the MLX layout above)
+ * into the device-resident tile layout the qmm kernels read (K0). The handle
+ * owns its device memory until aex_qweight_destroy. Reference: weight upload
+ * DirectDiTStep.quant / loadBlocks (Sources/ImarelloDirect/DirectDiTStep.swift:
+ * 278-335) and TransformerWeights.loadQuantized
+ * (Sources/ImarelloDiT/TransformerWeights.swift:13-54). */
+int aex_qweight_create(aex_ctx* ctx, const uint32_t* packed, const uint16_t* scales, const uint16_t* biases,
+                       int n, int k, int group_size, int bits, aex_qweight** out, aex_stream stream);
+void aex_qweight_destroy(aex_qweight* w);
+int aex_qweight_shape(const aex_qweight* w, int* n, int* k);
+
+/* Dequantize a tile-layout weight back to row-major bf16 [n, k] (bit-exact
+ * with aex_dequantize_mlx on the source). */
+int aex_qweight_dequantize(aex_ctx* ctx, const aex_qweight* w, uint16_t* out, aex_stream stream);
+
+#define AEX_DTYPE_BF16 0
+#define AEX_DTYPE_F32 1
+
+/* y[m, n] = x[m, k] . deq(W)[n, k]^T, x bf16 (row pitch ldx elements), y bf16
+ * or f32 (row pitch ldy), f32 accumulation. Reference: AttentionUtils.applyLinear
+ * -> quantizedMM(transpose: true, groupSize: 64, bits: 4)
+ * (Sources/ImarelloDiT/AttentionUtils.swift:140-230) and the direct engine's
+ * qmm dispatch (Sources/ImarelloDirect/DirectDiTStep.swift:374-406). */
+int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
+            int y_dtype, aex_stream stream);
+
+/* -------------------------------------------------------------- self test */
+
+/* Tensor-core path self test (no reference counterpart; a device bring-up
+ * check like the reference's `direct-spike` ladder, ImarelloCLI.swift:1701-1805).
+ * d[128, n] (f32) = a[128, 128] . op(b), a bf16 row-major;
+ * mode 0: b is [n, 128] (K-major), op(b) = b^T, operands from shared memory;
+ * mode 1: b is [128, n] (N-major), op(b) = b, A operand from tensor memory;
+ * mode 2: b is [128, n] (N-major), op(b) = b, operands from shared memory.
+ * n must be 128 or 256 (256 only for mode 0). Device pointers. */
+int aex_selftest_umma(aex_ctx* ctx, int mode, const uint16_t* a, const uint16_t* b, int n, float* d,
+                      aex_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AESTRIX_CUDA_H */
