@@ -1,0 +1,180 @@
+"""Parity of the fused joint attention (aex_joint_attention, through the C ABI)
+with the CPU oracle (fp32 composition RMSNorm -> interleaved RoPE -> softmax(sQK^T)V).
+
+Tolerance (north star): relative L2 <= 1e-2 and max-abs <= 2e-2 against the fp32
+reference evaluated on the same bf16-rounded inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+from aestrix_b200 import _lib, attention
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2
+ABS_TOL = 2e-2
+
+
+def _inputs(b, s, h, seed, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = ((torch.randn(b, s, h, 128, generator=g) * scale).to(dtype) for _ in range(3))
+    return q, k, v
+
+
+def _norm_weights(seed):
+    g = torch.Generator().manual_seed(seed)
+    return (1 + 0.1 * torch.randn(128, generator=g)).float(), (1 + 0.1 * torch.randn(128, generator=g)).float()
+
+
+def _rope(l_txt, grid_h, grid_w, text_positions="zero"):
+    txt = np.zeros((l_txt, 4), np.float32) if text_positions == "zero" else O.text_ids(l_txt)
+    ids = np.concatenate([txt, O.grid_ids(grid_h, grid_w)], 0)
+    return O.rope_freqs(ids, 2000.0)
+
+
+def _compare(got, ref, rows=None):
+    got = got.float().cpu().numpy()
+    if rows is not None:
+        got, ref = got[:, rows], ref[:, rows]
+    assert np.isfinite(got).all()
+    rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    mx = float(np.abs(got - ref).max())
+    assert rel <= REL_TOL and mx <= ABS_TOL, f"rel-L2 {rel:.3e} max-abs {mx:.3e}"
+    return rel, mx
+
+
+def _run_joint(q, k, v, wq, wk, eps, cos, sin):
+    dev = torch.device("cuda")
+    t = lambda a: None if a is None else (a if torch.is_tensor(a) else torch.from_numpy(a)).to(dev)
+    out = attention.joint_attention(t(q), t(k), t(v), t(wq), t(wk), eps, t(cos), t(sin))
+    torch.cuda.synchronize()
+    return out
+
+
+# --- ports of Tests/ImarelloDiTTests/MetalFlashAttentionTests.swift (D=128 cases) ----------------------
+@pytest.mark.parametrize("s,scale,seed", [(64, 0.1, 1), (64, 0.05, 6), (48, 1.0, 0), (128, 1.0, 3)])
+def test_sdpa_reference_cases(cuda_ctx, s, scale, seed):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = ((torch.randn(1, 2, s, 128, generator=g) * scale).to(torch.bfloat16) for _ in range(3))
+    out = attention.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    perm = lambda a: a.float().permute(0, 2, 1, 3).contiguous().numpy()
+    ref = O.sdpa(perm(q), perm(k), perm(v), 1 / np.sqrt(128))
+    got = out.permute(0, 2, 1, 3)
+    _compare(got, ref)
+    # the reference's own tighter bounds for these shapes hold for the bf16 path at these scales
+    if scale <= 0.1:
+        assert np.abs(got.float().cpu().numpy() - ref).max() < (5e-3 if scale == 0.1 else 1e-2)
+
+
+# --- BASELINE configs 1 and 2 (512^2 and 1024^2), sampled query rows ------------------------------------
+@pytest.mark.parametrize("grid,seed", [(32, 11), (64, 12)])
+def test_joint_attention_baseline_configs(cuda_ctx, grid, seed):
+    l_txt = 512
+    s = l_txt + grid * grid
+    q, k, v = _inputs(1, s, 24, seed)
+    wq, wk = _norm_weights(seed + 100)
+    cos, sin = _rope(l_txt, grid, grid)
+    out = _run_joint(q, k, v, wq, wk, 1e-6, cos, sin)
+    rows = np.r_[0:64, l_txt - 32:l_txt + 32, s - 64:s]
+    ref = np.full((1, s, 24, 128), np.nan, np.float32)
+    for lo, hi in ((0, 64), (l_txt - 32, l_txt + 32), (s - 64, s)):
+        part = O.joint_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), wq.numpy(), wk.numpy(),
+                                 1e-6, cos, sin, q_begin=lo, q_end=hi)
+        ref[:, lo:hi] = part[:, lo:hi]
+    _compare(out, ref, rows)
+
+
+# --- ragged lengths, reference eps / text ids, layouts -------------------------------------------------
+@pytest.mark.parametrize("s", [1, 48, 130, 200, 257, 384, 1000])
+def test_joint_attention_ragged(cuda_ctx, s):
+    q, k, v = _inputs(1, s, 3, 1000 + s)
+    wq, wk = _norm_weights(s)
+    g = torch.Generator().manual_seed(s)
+    theta = torch.rand(s, 64, generator=g).numpy() * 6.2831853
+    cos, sin = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+    out = _run_joint(q, k, v, wq, wk, 1e-5, cos, sin)
+    ref = O.joint_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), wq.numpy(), wk.numpy(),
+                            1e-5, cos, sin)
+    _compare(out, ref)
+
+
+def test_joint_attention_batch_and_text_ids(cuda_ctx):
+    l_txt, gh, gw = 64, 8, 24  # non-square grid, reference text ids [0,0,0,i]
+    s = l_txt + gh * gw
+    q, k, v = _inputs(3, s, 4, 77, scale=2.0)
+    wq, wk = _norm_weights(78)
+    cos, sin = _rope(l_txt, gh, gw, text_positions="ids")
+    out = _run_joint(q, k, v, wq, wk, 1e-5, cos, sin)
+    ref = O.joint_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), wq.numpy(), wk.numpy(),
+                            1e-5, cos, sin)
+    _compare(out, ref)
+
+
+def test_norm_only_rope_only_and_plain(cuda_ctx):
+    s = 300
+    q, k, v = _inputs(1, s, 2, 5)
+    wq, wk = _norm_weights(6)
+    cos, sin = _rope(44, 16, 16)
+    qf, kf, vf = (a.float().numpy() for a in (q, k, v))
+    for args in ((wq, wk, None, None), (None, None, cos, sin), (wq, None, None, None), (None, None, None, None)):
+        out = _run_joint(q, k, v, args[0], args[1], 1e-6, args[2], args[3])
+        ref = O.joint_attention(qf, kf, vf, None if args[0] is None else args[0].numpy(),
+                                None if args[1] is None else args[1].numpy(), 1e-6, args[2], args[3])
+        _compare(out, ref)
+
+
+def test_strided_output_into_concat_buffer(cuda_ctx):
+    """O written with the 12288-element row pitch of the single-stream concat
+    buffer (DirectDiTStep.swift:612-615); the MLP half must stay untouched."""
+    s, h = 260, 24
+    q, k, v = _inputs(1, s, h, 21)
+    wq, wk = _norm_weights(22)
+    cos, sin = _rope(4, 16, 16)
+    dev = torch.device("cuda")
+    concat = torch.full((1, s, 12288), 7.0, dtype=torch.bfloat16, device=dev)
+    out_view = concat[:, :, :3072].view(1, s, h, 128)
+    attention.joint_attention(q.to(dev), k.to(dev), v.to(dev), wq.to(dev), wk.to(dev), 1e-6,
+                              torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev), out=out_view)
+    torch.cuda.synchronize()
+    ref = O.joint_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), wq.numpy(), wk.numpy(), 1e-6,
+                            cos, sin)
+    _compare(out_view, ref)
+    assert bool((concat[:, :, 3072:] == 7.0).all())
+
+
+def test_bhsd_layout_matches_bshd(cuda_ctx):
+    q, k, v = (t.cuda() for t in _inputs(2, 200, 4, 31))
+    a = attention.joint_attention(q, k, v)
+    b = attention.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b.transpose(1, 2))
+
+
+def test_deterministic(cuda_ctx):
+    q, k, v = (t.cuda() for t in _inputs(1, 1536, 24, 41))
+    wq, wk = (w.cuda() for w in _norm_weights(42))
+    cos, sin = (torch.from_numpy(t).cuda() for t in _rope(512, 32, 32))
+    a = attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin)
+    b = attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert cuda_ctx.device_status() == 0
+
+
+def test_invalid_arguments_launch_nothing(cuda_ctx):
+    q = torch.zeros(1, 16, 2, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.AexError) as e:
+        attention.joint_attention(q, q, q)
+    assert e.value.code == _lib.AEX_ERR_UNSUPPORTED
+    q = torch.zeros(1, 16, 2, 132, dtype=torch.bfloat16, device="cuda")[..., :128]  # row pitch 132: not 16B
+    with pytest.raises(_lib.AexError) as e:
+        attention.joint_attention(q, q, q)
+    assert e.value.code == _lib.AEX_ERR_INVALID_ARG
+    q = torch.zeros(1, 16, 2, 128, dtype=torch.bfloat16, device="cuda")
+    cos = torch.zeros(16, 64, device="cuda")
+    with pytest.raises(_lib.AexError) as e:
+        attention.joint_attention(q, q, q, cos=cos, sin=None)
+    assert e.value.code == _lib.AEX_ERR_INVALID_ARG
