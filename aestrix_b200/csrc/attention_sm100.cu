@@ -9,22 +9,25 @@
 // 408-488).
 //
 // Two kernels:
-//  * qk_prep_kernel — one warp per (operand, batch, token, head) row: f32
+//  * qk_prep_kernel — one half-warp per (operand, batch, token, head) row: f32
 //    RMSNorm over the 128-wide head with the learned weight, then the
 //    interleaved-pair rotation with the row's cos/sin, rounded once to bf16
 //    into head-major scratch [B][H][S][128] (TMA-friendly: a 128-row tile is
 //    one contiguous 32 KB block). HBM-bound.
-//  * attn_fwd_kernel — one CTA per (256 query rows, head, batch), 10 warps:
-//      warps 0-3  softmax warpgroup of query tile 0 (one query row per thread)
-//      warps 4-7  softmax warpgroup of query tile 1
-//      warp 8     TMA producer (Q tiles once, K/V blocks through a 4-slot ring)
-//      warp 9     UMMA issuer (one thread)
+//  * attn_fwd_kernel — one CTA per (256 query rows, head, batch), 12 warps:
+//      warps 0-3   softmax warpgroup of query tile 0 (one query row per thread)
+//      warps 4-7   softmax warpgroup of query tile 1
+//      warp 8      TMA producer (Q tiles once, K/V blocks through a 4-slot ring)
+//      warp 9      UMMA issuer (one thread)
+//      warps 10-11 idle (complete the control warpgroup for setmaxnreg)
 //    Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,384),
 //    O1 [384,512). P_t is written as packed bf16 over the first 64 columns of
 //    S_t and consumed from tensor memory by the P.V UMMA. While one warpgroup
 //    runs its softmax the tensor core works on the other tile (ping-pong).
 //    Rescaling of O is lazy: the running max only moves when a block's max
-//    exceeds it by more than 2^8, so most blocks skip the O round trip.
+//    exceeds it by more than 2^8, so most blocks skip the O round trip. P is
+//    handed to the UMMA warp in two halves so P.V starts on keys 0-63 while
+//    the exponentials of keys 64-127 are still being computed.
 //    The epilogue divides by the row sum, stages the tile in the (now free) Q
 //    buffer with the 128-byte swizzle and writes it with TMA stores, so any
 //    output row pitch that is a multiple of 16 bytes works (e.g. the 12288-wide
@@ -44,21 +47,47 @@ constexpr int kTiles = 2;
 constexpr int kStages = 4;
 constexpr int kTileBytes = kBM * kD * 2;  // 32 KB, two 16 KB swizzle regions of 64 columns
 constexpr int kRegionBytes = kTileBytes / 2;
-constexpr int kThreads = 320;
+// 12 warps = 3 warpgroups: two softmax warpgroups (one query row per thread)
+// and one control warpgroup (TMA producer warp, UMMA warp, two idle warps).
+// Launched at 168 registers per thread (the per-sub-partition limit with 3
+// warps each); the control warpgroup then gives registers to the softmax
+// warpgroups: 64 + 2 * 216 = 496 <= 3 * 168 = 504.
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = (kSoftmaxWarps + 4) * 32;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kCtrlRegs = 64;
+constexpr int kSoftmaxRegs = 216;
+static_assert(kCtrlRegs + 2 * kSoftmaxRegs <= 3 * 168, "register split exceeds the launch allocation");
+
+// Tuning knobs (compile-time).
+// Of every 16 exponential pairs, how many use the FMA-pipe polynomial
+// (exp2_poly2) instead of MUFU ex2. Measured on B200 at 1024^2: 0 is fastest
+// (0.202 ms vs 0.208 ms at 4 and 0.223 ms at 8): the softmax is bound by
+// instruction issue of its single warp per sub-partition, not by MUFU.
+#ifndef AEX_ATTN_POLY_PAIRS
+#define AEX_ATTN_POLY_PAIRS 0
+#endif
+#ifndef AEX_ATTN_SPLIT_P
+#define AEX_ATTN_SPLIT_P 1  // hand P to the UMMA warp in two halves (keys 0-63, 64-127)
+#endif
+#ifndef AEX_ATTN_PIPE_LD
+#define AEX_ATTN_PIPE_LD 1  // overlap the S loads from tensor memory with the row-max computation
+#endif
+constexpr int kPolyPairs = AEX_ATTN_POLY_PAIRS;
+constexpr bool kSplitP = AEX_ATTN_SPLIT_P != 0;
 
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kTiles * kTileBytes;
 constexpr int kOffBar = kOffKV + kStages * kTileBytes;
 // barrier indices
-constexpr int kBarQFull = 0;                      // [2]
-constexpr int kBarKVFull = 2;                     // [kStages]
-constexpr int kBarKVEmpty = kBarKVFull + kStages; // [kStages]
-constexpr int kBarSFull = kBarKVEmpty + kStages;  // [2]
-constexpr int kBarPFull = kBarSFull + 2;          // [2]
-constexpr int kBarOFull = kBarPFull + 2;          // [2]
-constexpr int kBarDrain = kBarOFull + 2;          // [1]
+constexpr int kBarQFull = 0;                       // [2]
+constexpr int kBarKVFull = 2;                      // [kStages]
+constexpr int kBarKVEmpty = kBarKVFull + kStages;  // [kStages]
+constexpr int kBarSFull = kBarKVEmpty + kStages;   // [2]  S_t ready (UMMA commit)
+constexpr int kBarPFull = kBarSFull + 2;           // [2 tile][2 half] P_t half written (4 warps)
+constexpr int kBarOFull = kBarPFull + 4;           // [2]  O_t final (UMMA commit)
+constexpr int kBarDrain = kBarOFull + 2;           // [1]
 constexpr int kNumBars = kBarDrain + 1;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
 
@@ -70,10 +99,6 @@ struct Params {
   int n_kv;
   float scale_log2;
 };
-
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -94,16 +119,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bars[kBarQFull + 0], 1);
-    mbar_init(&bars[kBarQFull + 1], 1);
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(&bars[kBarQFull + t], 1);
+      mbar_init(&bars[kBarSFull + t], 1);
+      mbar_init(&bars[kBarPFull + 2 * t], 4);
+      mbar_init(&bars[kBarPFull + 2 * t + 1], 4);
+      mbar_init(&bars[kBarOFull + t], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kBarKVFull + s], 1);
       mbar_init(&bars[kBarKVEmpty + s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&bars[kBarSFull + t], 1);
-      mbar_init(&bars[kBarPFull + t], 4);  // one arrive per softmax warp
-      mbar_init(&bars[kBarOFull + t], 1);
     }
     mbar_init(&bars[kBarDrain], 1);
     fence_barrier_init();
@@ -122,10 +147,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
+  // Each role's code sits inside the branch that set its register budget, so
+  // ptxas compiles the softmax and the control warps with their own limits.
+  if (warp >= kSoftmaxWarps) {
+    regs_dealloc<kCtrlRegs>();
+    if (warp == kProducerWarp && lane == 0) {
+      // ---------------------------------------------------------- producer
       for (int t = 0; t < kTiles; ++t) {
         uint8_t* dst = smem + kOffQ + t * kTileBytes;
         mbar_arrive_expect_tx(&bars[kBarQFull + t], kTileBytes);
@@ -149,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (abort_flag) {
         // Let every copy already issued land before the CTA releases its
-        // shared memory (bounded: the waits themselves time out).
+        // shared memory (bounded: each wait gives up after the timeout).
         for (int idx = (issued > kStages ? issued - kStages : 0); idx < issued; ++idx) {
           const uint32_t a = smem_u32(&bars[kBarKVFull + idx % kStages]);
           const uint64_t t0 = globaltimer_ns();
@@ -157,30 +184,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ UMMA issue
-    if (lane == 0) {
+    } else if (warp == kMmaWarp && lane == 0) {
+      // ---------------------------------------------------------- UMMA issue
       bool ok = mbar_wait(&bars[kBarQFull + 0], 0, &abort_flag, status, kDevTimeoutMma) &&
                 mbar_wait(&bars[kBarQFull + 1], 0, &abort_flag, status, kDevTimeoutMma);
       const uint32_t sQ = smem_u32(smem + kOffQ);
       const uint32_t sKV = smem_u32(smem + kOffKV);
+      // Descriptors are built once; advancing along K adds the byte offset / 16
+      // to the start-address field (all offsets stay inside the 14-bit field).
+      const uint64_t dq = sdesc_sw128(sQ, 16, 1024);
+      const uint64_t dkv_k = sdesc_sw128(sKV, 16, 1024);
+      const uint64_t dkv_v = sdesc_sw128(sKV, kRegionBytes, 1024);
       auto issue_s = [&](int t, int slot) {
-        const uint32_t qa = sQ + t * kTileBytes;
-        const uint32_t ka = sKV + slot * kTileBytes;
-#pragma unroll
+        const uint64_t qa = dq + ((t * kTileBytes) >> 4);
+        const uint64_t ka = dkv_k + ((slot * kTileBytes) >> 4);
+#pragma unroll 1
         for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kRegionBytes + (kk & 3) * 32;
-          umma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), kIdescS,
-                  kk > 0);
+          const uint32_t off = ((kk >> 2) * kRegionBytes + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + t * 128, qa + off, ka + off, kIdescS, kk > 0);
         }
       };
-      auto issue_pv = [&](int t, int slot, bool accumulate) {
-        const uint32_t va = sKV + slot * kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, sdesc_sw128(va + kk * 2048, kRegionBytes, 1024),
-                  kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
+      // P_t[j].V for key steps [kk0, kk1) (16 keys each).
+      auto issue_pv = [&](int t, int slot, bool accumulate, int kk0, int kk1) {
+        const uint64_t va = dkv_v + ((slot * kTileBytes) >> 4);
+#pragma unroll 1
+        for (int kk = kk0; kk < kk1; ++kk)
+          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, va + ((kk * 2048) >> 4), kIdescPV,
+                  (accumulate || kk > 0) ? 1u : 0u);
+      };
+      // Waits for P_t of block `jj` (one or two halves) and issues its P.V.
+      auto wait_p_issue_pv = [&](int t, int slot, int jj) -> bool {
+        if (kSplitP) {
+          if (!mbar_wait(&bars[kBarPFull + 2 * t], jj & 1, &abort_flag, status, kDevTimeoutMma)) return false;
+          tc_fence_after();
+          issue_pv(t, slot, jj > 0, 0, 4);
+          if (!mbar_wait(&bars[kBarPFull + 2 * t + 1], jj & 1, &abort_flag, status, kDevTimeoutMma)) return false;
+          tc_fence_after();
+          issue_pv(t, slot, true, 4, 8);
+        } else {
+          if (!mbar_wait(&bars[kBarPFull + 2 * t + 1], jj & 1, &abort_flag, status, kDevTimeoutMma)) return false;
+          tc_fence_after();
+          issue_pv(t, slot, jj > 0, 0, 8);
+        }
+        return true;
       };
       if (ok) ok = mbar_wait(&bars[kBarKVFull + 0], 0, &abort_flag, status, kDevTimeoutMma);
       if (ok) {
@@ -197,10 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(&bars[kBarKVFull + kslot], (kidx / kStages) & 1, &abort_flag, status, kDevTimeoutMma) &&
              mbar_wait(&bars[kBarKVFull + vslot], (vidx / kStages) & 1, &abort_flag, status, kDevTimeoutMma);
         for (int t = 0; t < kTiles && ok; ++t) {
-          ok = mbar_wait(&bars[kBarPFull + t], (j - 1) & 1, &abort_flag, status, kDevTimeoutMma);
+          // P_t[j-1].V (reads P from tensor memory), then S_t[j] overwrites
+          // the same columns: UMMAs issued by one thread execute in order.
+          ok = wait_p_issue_pv(t, vslot, j - 1);
           if (!ok) break;
-          tc_fence_after();
-          issue_pv(t, vslot, j - 1 > 0);
           issue_s(t, kslot);
           umma_commit(&bars[kBarSFull + t]);
         }
@@ -214,10 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int vslot = vidx % kStages;
         ok = mbar_wait(&bars[kBarKVFull + vslot], (vidx / kStages) & 1, &abort_flag, status, kDevTimeoutMma);
         for (int t = 0; t < kTiles && ok; ++t) {
-          ok = mbar_wait(&bars[kBarPFull + t], (n_kv - 1) & 1, &abort_flag, status, kDevTimeoutMma);
+          ok = wait_p_issue_pv(t, vslot, n_kv - 1);
           if (!ok) break;
-          tc_fence_after();
-          issue_pv(t, vslot, n_kv - 1 > 0);
           umma_commit(&bars[kBarOFull + t]);
         }
       }
@@ -226,40 +270,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&bars[kBarDrain], 0, &abort_flag, status, kDevTimeoutMma);
     }
   } else {
+    regs_alloc<kSoftmaxRegs>();
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;
     const int quad = warp & 3;
+    const int row = quad * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem + lane_base + t * 128;
     const uint32_t tO = tmem + lane_base + 256 + t * 128;
+    const uint32_t bar_s = smem_u32(&bars[kBarSFull + t]);
+    const uint32_t bar_p = smem_u32(&bars[kBarPFull + 2 * t]);
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      ok = mbar_wait(&bars[kBarSFull + t], j & 1, &abort_flag, status, kDevTimeoutSoftmax);
+      ok = mbar_wait_addr(bar_s, j & 1, &abort_flag, status, kDevTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t r[128];
-      tmem_ld32(tS + 0, r + 0);
-      tmem_ld32(tS + 32, r + 32);
-      tmem_ld32(tS + 64, r + 64);
-      tmem_ld32(tS + 96, r + 96);
-      tmem_wait_ld();
       const int valid = p.seq - j * kBN;
-      if (valid < kBN) {
+      float mx0, mx1, mx2, mx3;
+      auto mask_chunk = [&](int c0) {
+        if (valid < kBN) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= valid) r[i] = __float_as_uint(-INFINITY);
-      }
-      float mx0 = __uint_as_float(r[0]), mx1 = __uint_as_float(r[1]);
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i >= valid) r[c0 + i] = __float_as_uint(-INFINITY);
+        }
+      };
+      auto max_chunk = [&](int c0) {  // 32 columns into the four chains
 #pragma unroll
-      for (int i = 2; i < 128; i += 2) {
-        mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-        mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
+        for (int i = 0; i < 32; i += 8) {
+          mx0 = fmax3(mx0, __uint_as_float(r[c0 + i]), __uint_as_float(r[c0 + i + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(r[c0 + i + 2]), __uint_as_float(r[c0 + i + 3]));
+          mx2 = fmax3(mx2, __uint_as_float(r[c0 + i + 4]), __uint_as_float(r[c0 + i + 5]));
+          mx3 = fmax3(mx3, __uint_as_float(r[c0 + i + 6]), __uint_as_float(r[c0 + i + 7]));
+        }
+      };
+      mx0 = mx1 = mx2 = mx3 = -INFINITY;
+      if (AEX_ATTN_PIPE_LD) {
+        // Each wait covers the chunk just issued; the max of the previous
+        // chunk is computed while the next one is in flight.
+        tmem_ld32(tS + 0, r + 0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          if (c0 + 32 < 128) tmem_ld32(tS + c0 + 32, r + c0 + 32);
+          mask_chunk(c0);
+          max_chunk(c0);
+          if (c0 + 32 < 128) tmem_wait_ld();
+        }
+      } else {
+        tmem_ld32(tS + 0, r + 0);
+        tmem_ld32(tS + 32, r + 32);
+        tmem_ld32(tS + 64, r + 64);
+        tmem_ld32(tS + 96, r + 96);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          mask_chunk(c0);
+          max_chunk(c0);
+        }
       }
-      const float m_blk = fmaxf(mx0, mx1) * sl2;
+      const float m_blk = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+      // Lazy rescale: the reference max only moves when the block max exceeds
+      // it by more than 8 (a factor 2^8), so P stays <= 256.
       float alpha = 1.f;
       bool rescale = false;
       if (m_blk > m_run + 8.f) {
@@ -268,66 +344,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         rescale = (j > 0);
       }
       l_run *= alpha;
-      const float neg_m = -m_run;
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(r[c * 32 + 2 * i]), sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(r[c * 32 + 2 * i + 1]), sl2, neg_m));
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(tS + c * 16, pk);
-      }
-      l_run += sum0 + sum1;
       if (__any_sync(0xffffffffu, rescale)) {
+        // O_t holds P.V of blocks < j (its UMMAs completed before S_t[j]).
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
+        for (int cc = 0; cc < 128; cc += 32) {
           uint32_t o[32];
-          tmem_ld32(tO + c, o);
+          tmem_ld32(tO + cc, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + c, o);
+          tmem_st32(tO + cc, o);
         }
       }
+      const float2 sl2x2 = make_float2(sl2, sl2);
+      const float2 negm2 = make_float2(-m_run, -m_run);
+      float2 sum_a = make_float2(0.f, 0.f), sum_b = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = ffma2(make_float2(__uint_as_float(r[ch * 32 + 2 * i]),
+                                             __uint_as_float(r[ch * 32 + 2 * i + 1])),
+                                 sl2x2, negm2);
+          // kPolyPairs of every 16 pairs on the FMA pipe, the rest on MUFU.
+          const float2 pe = (i < kPolyPairs) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          if (i & 1)
+            sum_b = fadd2(sum_b, pe);
+          else
+            sum_a = fadd2(sum_a, pe);
+          pk[i] = pack_bf16x2(pe.x, pe.y);
+        }
+        tmem_st16(tS + ch * 16, pk);
+        if (ch == 1 && kSplitP) {
+          // keys 0-63 of P are in tensor memory: the UMMA warp may start P.V
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_addr(bar_p);
+        }
+      }
+      l_run += (sum_a.x + sum_a.y) + (sum_b.x + sum_b.y);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kBarPFull + t]);
+      if (lane == 0) mbar_arrive_addr(bar_p + 8);
     }
     // ------------------------------------------------------------ epilogue
     if (ok) ok = mbar_wait(&bars[kBarOFull + t], 0, &abort_flag, status, kDevTimeoutEpilogue);
     ok = __all_sync(0xffffffffu, ok);
     uint8_t* stage = smem + kOffQ + t * kTileBytes;  // Q_t is dead once O_t is final
-    const int row = quad * 32 + lane;
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+      for (int cc = 0; cc < 128; cc += 32) {
         uint32_t o[32];
-        tmem_ld32(tO + c, o);
+        tmem_ld32(tO + cc, o);
         tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
-        uint8_t* rowp = stage + (c >> 6) * kRegionBytes + row * 128;
+        // columns [cc, cc+32) live in swizzle region cc/64, 16-byte chunks (cc%64)/8 .. +4
+        uint8_t* rowp = stage + (cc >> 6) * kRegionBytes + row * 128;
 #pragma unroll
         for (int qd = 0; qd < 4; ++qd) {
-          const int chunk = (((c & 63) >> 3) + qd) ^ (row & 7);
+          const int chunk = (((cc & 63) >> 3) + qd) ^ (row & 7);
           *reinterpret_cast<uint4*>(rowp + chunk * 16) =
               make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
         }
       }
       fence_async_shared();
     }
-    named_bar_sync(1 + t, 128);
+    // The four warps of this tile have staged their rows (bounded: the
+    // warps of a tile reach this point together or all abort).
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(128) : "memory");
     if (ok && quad == 0 && lane == 0 && q0 + t * kBM < p.seq) {
       tma_store_4d(&tm_o, stage, 0, q0 + t * kBM, h, b);
       tma_store_4d(&tm_o, stage + kRegionBytes, 64, q0 + t * kBM, h, b);
@@ -358,46 +450,87 @@ struct PrepParams {
   __nv_bfloat16* out;  // [2][B][H][S][128]
 };
 
+// Each half-warp owns one 128-wide row (16 lanes x 8 elements = one 16-byte
+// load per lane); a warp keeps kPrepRowsPerWarp rows in flight so every lane
+// has several independent 16-byte loads outstanding (HBM-bound kernel).
+constexpr int kPrepRowsPerWarp = 8;
+constexpr int kPrepWarps = 8;
+
 __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
-  const int64_t rows_per_op = static_cast<int64_t>(p.batch) * p.seq * p.heads;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= 2 * rows_per_op) return;
+  // 32-bit index math: the host guarantees 2*B*S*H < 2^31.
+  const uint32_t rows_per_op = static_cast<uint32_t>(p.batch) * p.seq * p.heads;
+  const uint32_t total = 2 * rows_per_op;
+  const uint32_t heads = p.heads, seq = p.seq;
   const int lane = threadIdx.x & 31;
-  const int which = row >= rows_per_op ? 1 : 0;
-  const int64_t r = row - which * rows_per_op;
-  const int hh = static_cast<int>(r % p.heads);
-  const int s = static_cast<int>((r / p.heads) % p.seq);
-  const int bb = static_cast<int>(r / (static_cast<int64_t>(p.heads) * p.seq));
-  const __nv_bfloat16* src = which ? p.k + bb * p.k_sb + s * p.k_ss + hh * p.k_sh
-                                   : p.q + bb * p.q_sb + s * p.q_ss + hh * p.q_sh;
-  const float* w = which ? p.wk : p.wq;
-  const uint2 raw = *reinterpret_cast<const uint2*>(src + lane * 4);
-  float x0 = bf16lo_to_f32(raw.x), x1 = bf16hi_to_f32(raw.x);
-  float x2 = bf16lo_to_f32(raw.y), x3 = bf16hi_to_f32(raw.y);
-  if (w) {
-    float ss = x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3;
+  const int half = lane >> 4;  // which row of the pair
+  const int l16 = lane & 15;   // 8-element slice of the row
+  const uint32_t warp_row0 = (blockIdx.x * kPrepWarps + (threadIdx.x >> 5)) * kPrepRowsPerWarp;
+  uint4 raw[kPrepRowsPerWarp / 2];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss * (1.0f / kD) + p.eps);
-    const float4 wv = *reinterpret_cast<const float4*>(w + lane * 4);
-    x0 = x0 * inv * wv.x;
-    x1 = x1 * inv * wv.y;
-    x2 = x2 * inv * wv.z;
-    x3 = x3 * inv * wv.w;
+  for (int it = 0; it < kPrepRowsPerWarp / 2; ++it) {
+    const uint32_t row = warp_row0 + 2 * it + half;
+    raw[it] = make_uint4(0, 0, 0, 0);
+    if (row < total) {
+      const uint32_t which = row >= rows_per_op ? 1 : 0;
+      const uint32_t r = row - which * rows_per_op;
+      const int64_t hh = r % heads;
+      const int64_t s = (r / heads) % seq;
+      const int64_t bb = r / (heads * seq);
+      const __nv_bfloat16* src = which ? p.k + bb * p.k_sb + s * p.k_ss + hh * p.k_sh
+                                       : p.q + bb * p.q_sb + s * p.q_ss + hh * p.q_sh;
+      raw[it] = __ldg(reinterpret_cast<const uint4*>(src) + l16);
+    }
   }
-  if (p.cos_t) {
-    const float2 c = *reinterpret_cast<const float2*>(p.cos_t + static_cast<int64_t>(s) * (kD / 2) + lane * 2);
-    const float2 sn = *reinterpret_cast<const float2*>(p.sin_t + static_cast<int64_t>(s) * (kD / 2) + lane * 2);
-    const float y0 = x0 * c.x - x1 * sn.x, y1 = x1 * c.x + x0 * sn.x;
-    const float y2 = x2 * c.y - x3 * sn.y, y3 = x3 * c.y + x2 * sn.y;
-    x0 = y0;
-    x1 = y1;
-    x2 = y2;
-    x3 = y3;
+#pragma unroll
+  for (int it = 0; it < kPrepRowsPerWarp / 2; ++it) {
+    const uint32_t row = warp_row0 + 2 * it + half;
+    const bool valid = row < total;
+    const uint32_t which = row >= rows_per_op ? 1 : 0;
+    const uint32_t r = row - which * rows_per_op;
+    const int64_t hh = r % heads;
+    const int64_t s = (r / heads) % seq;
+    const int64_t bb = r / (heads * seq);
+    float x[8];
+    const uint32_t wv4[4] = {raw[it].x, raw[it].y, raw[it].z, raw[it].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = bf16lo_to_f32(wv4[i]);
+      x[2 * i + 1] = bf16hi_to_f32(wv4[i]);
+    }
+    const float* w = which ? p.wk : p.wq;
+    // The two half-warps may hold rows of different operands (Q and K), so the
+    // reduction runs for every lane and only its use depends on `w`.
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (w) {
+      const float inv = rsqrtf(ss * (1.0f / kD) + p.eps);
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + l16 * 8));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + l16 * 8 + 4));
+      const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * wa[i];
+    }
+    if (p.cos_t && valid) {
+      const float4 c = __ldg(reinterpret_cast<const float4*>(p.cos_t + s * (kD / 2) + l16 * 4));
+      const float4 sn = __ldg(reinterpret_cast<const float4*>(p.sin_t + s * (kD / 2) + l16 * 4));
+      const float ca[4] = {c.x, c.y, c.z, c.w}, sa[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float re = x[2 * i], im = x[2 * i + 1];
+        x[2 * i] = re * ca[i] - im * sa[i];
+        x[2 * i + 1] = im * ca[i] + re * sa[i];
+      }
+    }
+    if (valid) {
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(which) * rows_per_op * kD +
+                           ((bb * heads + hh) * seq + s) * kD + l16 * 8;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                                                  pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+    }
   }
-  __nv_bfloat16* dst = p.out + which * rows_per_op * kD +
-                       ((static_cast<int64_t>(bb) * p.heads + hh) * p.seq + s) * kD + lane * 4;
-  *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(x0, x1), pack_bf16x2(x2, x3));
 }
 
 }  // namespace attn
@@ -484,8 +617,9 @@ int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratc
     pp.heads = H;
     pp.out = static_cast<__nv_bfloat16*>(scratch);
     const int64_t rows = 2ll * B * S * H;
-    const int64_t blocks = (rows + 7) / 8;
-    if (blocks > 0x7FFFFFFFll) return set_error(ctx, AEX_ERR_INVALID_ARG, "problem too large");
+    const int64_t per_block = attn::kPrepWarps * attn::kPrepRowsPerWarp;
+    const int64_t blocks = (rows + per_block - 1) / per_block;
+    if (rows >= (1ll << 31)) return set_error(ctx, AEX_ERR_INVALID_ARG, "batch*seq*heads too large");
     attn::qk_prep_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(pp);
     if (int r = check_launch(ctx, "qk_prep_kernel")) return r;
     const int64_t plane = static_cast<int64_t>(B) * H * S * 128;

@@ -1,0 +1,396 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 joint attention hot path.
+
+Workload (one "step"): the fused QK-RMSNorm -> 2-D axial RoPE -> non-causal SDPA of
+one FLUX.2-klein joint attention call at 1024^2: batch 1 per GPU, 24 heads x 128,
+512 text + 4096 image tokens (64x64 grid) = 4608 tokens, bf16, Q/K/V ~ N(0,1),
+norm weights 1+0.1*N(0,1), eps 1e-6, RoPE theta 2000 (text positions 0).
+Work per step = 4*S^2*D*H = 260.9 GFLOP.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank one image (batch-sharded
+replicas: no data-path collective, weak scaling); timing is on-device CUDA events,
+max over ranks; rank 0 prints one JSON line.
+
+`--impl reference` times the reference arm: the CPU restatement of the reference
+composition (oracle/, the reference itself is Swift/MLX/Metal and cannot run here) on
+this host's cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+L_TXT, GRID, HEADS, HEAD_DIM = 512, 64, 24, 128
+SEQ = L_TXT + GRID * GRID
+FLOPS_PER_CALL = 4.0 * SEQ * SEQ * HEAD_DIM * HEADS
+N_INPUT_SETS = 4  # 4 x (Q,K,V,O) = 453 MB > 126 MB L2: every step reads cold inputs
+METRIC = "joint_attention_tflops_1024"
+CONFIG = {
+    "workload": "joint_attention_1024 (BASELINE configs[1])",
+    "batch_per_gpu": 1,
+    "seq": SEQ,
+    "text_tokens": L_TXT,
+    "image_grid": f"{GRID}x{GRID}",
+    "heads": HEADS,
+    "head_dim": HEAD_DIM,
+    "fused": "qk_rmsnorm(eps 1e-6)+rope(theta 2000)+sdpa, non-causal",
+    "parallelism": "batch-sharded replicas (1 image per GPU)",
+    "l2": f"inputs rotate over {N_INPUT_SETS} sets (> L2), no flush needed",
+}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def _rope_tables():
+    """Text positions 0, image ids (0, h, w, 0) on the 64x64 grid (Flux2RoPE.prepareGridIDs)."""
+    ids = np.zeros((SEQ, 4), np.float32)
+    hh, ww = np.meshgrid(np.arange(GRID), np.arange(GRID), indexing="ij")
+    ids[L_TXT:, 1] = hh.reshape(-1)
+    ids[L_TXT:, 2] = ww.reshape(-1)
+    half = np.arange(16, dtype=np.float32)
+    omega = 1.0 / np.power(np.float32(2000.0), 2.0 * half / 32.0).astype(np.float32)
+    ang = np.concatenate([ids[:, a:a + 1] * omega[None, :] for a in range(4)], axis=1).astype(np.float32)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            # NVML initialisation can stall the GPU briefly: let it finish before any timing.
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 10:
+                time.sleep(0.02)
+            self.n_pre = len(self.lines)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def mark(self):
+        return len(self.lines)
+
+    def summary(self, since: int = 0):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines[since:]:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _traffic_from_profile():
+    path = os.path.join(ROOT, "profiles", "attn_fwd_1024.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+def cpu_baseline_sample(threads: int | None = None, rows: int = SEQ):
+    """Oracle (fp32 C++ restatement) on a bounded sample: `rows` query rows of all 24 heads
+    against all 4608 keys of the 1024^2 call. Returns (TFLOP/s, seconds, sample description, cores)."""
+    from oracle import oracle as O
+
+    if threads:
+        os.environ["AEXO_THREADS"] = str(threads)
+    cores = int(os.environ.get("AEXO_THREADS", os.cpu_count() or 1))
+    rng = np.random.default_rng(7)
+    q, k, v = (rng.standard_normal((1, SEQ, HEADS, HEAD_DIM), dtype=np.float32) for _ in range(3))
+    wq = (1 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32)
+    wk = (1 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32)
+    cos, sin = _rope_tables()
+    t0 = time.perf_counter()
+    O.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, q_begin=0, q_end=rows)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows * SEQ * HEAD_DIM * HEADS
+    return flops / dt / 1e12, dt, f"{rows} of {SEQ} query rows x {HEADS} heads, all keys, fp32", cores
+
+
+def run_reference(args):
+    """Reference arm: the CPU restatement of the reference composition on all host cores.
+
+    One step = the fused norm -> RoPE -> SDPA of one head (its own Q/K norm and RoPE, all
+    4608 keys) for a sample of its query rows; heads rotate over steps. The row count is
+    calibrated during warm-up so that all W + K steps take about --ref-seconds."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    cores = int(os.environ.get("AEXO_THREADS", os.cpu_count() or 1))
+    rng = np.random.default_rng(7)
+    q, k, v = (rng.standard_normal((1, SEQ, HEADS, HEAD_DIM), dtype=np.float32) for _ in range(3))
+    heads = [tuple(np.ascontiguousarray(a[:, :, h:h + 1]) for a in (q, k, v)) for h in range(HEADS)]
+    wq = (1 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32)
+    wk = (1 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32)
+    cos, sin = _rope_tables()
+
+    def ref_step(i, rows):
+        qh, kh, vh = heads[i % HEADS]
+        O.joint_attention(qh, kh, vh, wq, wk, 1e-6, cos, sin, q_begin=0, q_end=rows)
+
+    t0 = time.perf_counter()
+    ref_step(0, SEQ)
+    t_full = time.perf_counter() - t0
+    budget = args.ref_seconds / max(1, args.steps + args.warmup)
+    rows = int(min(SEQ, max(64, SEQ * budget / t_full)))
+    for i in range(args.warmup):
+        ref_step(i, rows)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        ref_step(i, rows)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows * SEQ * HEAD_DIM * args.steps
+    value = flops / dt / 1e12
+    sample = f"per step: 1 of {HEADS} heads (own RMSNorm+RoPE, all {SEQ} keys), {rows} of {SEQ} query rows, fp32"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": FLOPS_PER_CALL / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(CONFIG, reference="CPU restatement of the reference composition (oracle/aex_oracle.cpp); "
+                       "the reference's own Swift/MLX/Metal path is unavailable on this box"),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = _dist_init()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from aestrix_b200 import _lib, attention
+
+    ctx = _lib.context(local)
+    g = torch.Generator().manual_seed(1000 + rank)
+    sets = []
+    for _ in range(N_INPUT_SETS):
+        q, k, v = (torch.randn(1, SEQ, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+        sets.append((q, k, v, torch.empty_like(q)))
+    wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    wk = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    cos_np, sin_np = _rope_tables()
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        q, k, v, o = sets[i % N_INPUT_SETS]
+        attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, out=o, ctx=ctx, stream=stream)
+
+    clk = ClockSampler(local).__enter__()
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ctx.sync(stream.cuda_stream)
+
+    # ---- timed region: K fused calls (2 launches each: qk_prep + attn_fwd)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    clk_mark = clk.mark()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk_end = clk.mark()
+    _barrier(world)
+    clk.__exit__()
+    clocks = clk.summary(clk_mark) if clk_end > clk_mark else dict(clk.summary(clk.n_pre), note="timed region "
+                                                                   "shorter than the 100 ms sample period: "
+                                                                   "samples from warm-up through timing")
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = _max_over_ranks(world, ms_local)
+    ctx.sync(stream.cuda_stream)
+    value = world * FLOPS_PER_CALL / (ms * 1e-3) / 1e12
+
+    # ---- dominant kernel alone (attn_fwd_kernel: pre-normalized inputs, no prep launch)
+    for i in range(2):
+        q, k, v, o = sets[i % N_INPUT_SETS]
+        attention.joint_attention(q, k, v, out=o, ctx=ctx, stream=stream)
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_k = min(max(args.steps, 10), 400)
+    ka.record(stream)
+    for i in range(n_k):
+        q, k, v, o = sets[i % N_INPUT_SETS]
+        attention.joint_attention(q, k, v, out=o, ctx=ctx, stream=stream)
+    kb.record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = ka.elapsed_time(kb) / n_k
+    ctx.sync(stream.cuda_stream)
+
+    # ---- end to end through the C ABI with host buffers (H2D inputs, D2H output per step)
+    hq, hk, hv = (sets[0][j].cpu().pin_memory() for j in range(3))
+    hwq, hwk, hcos, hsin = (t.cpu().pin_memory() for t in (wq, wk, cos, sin))
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv, do = (torch.empty_like(sets[0][j]) for j in range(4))
+    dwq, dwk, dcos, dsin = (torch.empty_like(t) for t in (wq, wk, cos, sin))
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hwq, hwk, hcos, hsin))
+    d2h = ho.numel() * ho.element_size()
+
+    def e2e_step():
+        for d, h in ((dq, hq), (dk, hk), (dv, hv), (dwq, hwq), (dwk, hwk), (dcos, hcos), (dsin, hsin)):
+            d.copy_(h, non_blocking=True)
+        attention.joint_attention(dq, dk, dv, dwq, dwk, 1e-6, dcos, dsin, out=do, ctx=ctx, stream=stream)
+        ho.copy_(do, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e = max(3, min(args.steps, 10))
+    ea.record(stream)
+    for _ in range(n_e):
+        e2e_step()
+    eb.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(world, ea.elapsed_time(eb) / n_e)
+    _barrier(world)
+
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        achieved = FLOPS_PER_CALL / (kernel_ms * 1e-3) / 1e12
+        tf_cpu, dt_cpu, sample, cores = cpu_baseline_sample(rows=args.cpu_rows)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
+            "pct_bf16_peak": 100.0 * value / world / peak,
+            "roofline": {"bound": "tensor", "kernel": "attn_fwd_kernel", "achieved": achieved, "peak": peak,
+                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)", "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": _traffic_from_profile(),
+                         "algorithmic": f"{FLOPS_PER_CALL / 1e9:.1f} GFLOP per launch (4*S^2*D*H)",
+                         "kernel_ms": kernel_ms},
+            "cpu_baseline": {"value": tf_cpu, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample,
+                             "seconds": dt_cpu},
+            "e2e": {"value": world * FLOPS_PER_CALL / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "path": "aex_joint_attention via ctypes, pinned host buffers, copies on the same stream"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-rows", type=int, default=SEQ, help="query rows in the CPU-baseline sample")
+    ap.add_argument("--ref-seconds", type=float, default=90.0, help="target duration of the reference arm")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

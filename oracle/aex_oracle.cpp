@@ -196,36 +196,57 @@ void aexo_sdpa(const float* q, const float* k, const float* v, float* out, int b
   q_begin = std::max(0, q_begin);
   q_end = std::min(s, q_end);
   if (q_end <= q_begin) return;
+  // Blocks of kQB query rows share every key/value row while it is in cache.
+  constexpr int kQB = 32;
   const int nq = q_end - q_begin;
-  const int64_t total = (int64_t)b * h * nq;
-  parallel_for(total, 8, [&](int64_t job) {
-    thread_local std::vector<float> sc;
-    thread_local std::vector<double> acc;
-    sc.resize(s);
-    acc.resize(d);
-    {
-      const int qi = q_begin + static_cast<int>(job % nq);
-      const int hh = static_cast<int>((job / nq) % h);
-      const int bb = static_cast<int>(job / ((int64_t)nq * h));
-      const float* qr = q + bb * stride_b + (int64_t)qi * stride_s + hh * stride_h;
-      float mx = -INFINITY;
-      for (int j = 0; j < s; ++j) {
-        const float* kr = k + bb * stride_b + (int64_t)j * stride_s + hh * stride_h;
+  const int nblk = (nq + kQB - 1) / kQB;
+  const int64_t total = (int64_t)b * h * nblk;
+  parallel_for(total, 1, [&](int64_t job) {
+    thread_local std::vector<float> sc, acc;
+    sc.resize((size_t)kQB * s);
+    acc.resize((size_t)kQB * d);
+    const int blk = static_cast<int>(job % nblk);
+    const int hh = static_cast<int>((job / nblk) % h);
+    const int bb = static_cast<int>(job / ((int64_t)nblk * h));
+    const int i0 = q_begin + blk * kQB;
+    const int nb = std::min(kQB, q_end - i0);
+    const float* qrow[kQB];
+    for (int i = 0; i < nb; ++i) qrow[i] = q + bb * stride_b + (int64_t)(i0 + i) * stride_s + hh * stride_h;
+    for (int j = 0; j < s; ++j) {
+      const float* kr = k + bb * stride_b + (int64_t)j * stride_s + hh * stride_h;
+      for (int i = 0; i < nb; ++i) {
+        const float* qr = qrow[i];
         float dot = 0.f;
+#pragma omp simd reduction(+ : dot)
         for (int t = 0; t < d; ++t) dot += qr[t] * kr[t];
-        sc[j] = dot * scale;
-        mx = std::max(mx, sc[j]);
+        sc[(size_t)i * s + j] = dot * scale;
       }
-      double l = 0.0;
-      std::fill(acc.begin(), acc.end(), 0.0);
+    }
+    double l[kQB];
+    for (int i = 0; i < nb; ++i) {
+      float* row = &sc[(size_t)i * s];
+      float mx = -INFINITY;
+      for (int j = 0; j < s; ++j) mx = std::max(mx, row[j]);
+      double sum = 0.0;
       for (int j = 0; j < s; ++j) {
-        const float p = std::exp(sc[j] - mx);
-        l += p;
-        const float* vr = v + bb * stride_b + (int64_t)j * stride_s + hh * stride_h;
-        for (int t = 0; t < d; ++t) acc[t] += (double)p * vr[t];
+        row[j] = std::exp(row[j] - mx);
+        sum += row[j];
       }
-      float* orow = out + bb * stride_b + (int64_t)qi * stride_s + hh * stride_h;
-      for (int t = 0; t < d; ++t) orow[t] = static_cast<float>(acc[t] / l);
+      l[i] = sum;
+    }
+    std::fill(acc.begin(), acc.end(), 0.f);
+    for (int j = 0; j < s; ++j) {
+      const float* vr = v + bb * stride_b + (int64_t)j * stride_s + hh * stride_h;
+      for (int i = 0; i < nb; ++i) {
+        const float pij = sc[(size_t)i * s + j];
+        float* a = &acc[(size_t)i * d];
+#pragma omp simd
+        for (int t = 0; t < d; ++t) a[t] += pij * vr[t];
+      }
+    }
+    for (int i = 0; i < nb; ++i) {
+      float* orow = out + bb * stride_b + (int64_t)(i0 + i) * stride_s + hh * stride_h;
+      for (int t = 0; t < d; ++t) orow[t] = static_cast<float>(acc[(size_t)i * d + t] / l[i]);
     }
   });
 }
