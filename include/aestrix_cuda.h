@@ -130,8 +130,10 @@ size_t aex_joint_attention_scratch_bytes(const aex_attention_args* args);
 int aex_joint_attention_ws(aex_ctx* ctx, const aex_attention_args* args, void* scratch, size_t scratch_bytes,
                            aex_stream stream);
 
-/* 4-axis rotary tables. ids: [n, 4] f32 positions (t, h, w, l); out cos/sin:
- * [n, sum(axes_dim)/2] f32 (device pointers). Reference: Flux2PosEmbed
+/* Rotary tables. ids: [n, n_axes] f32 positions (FLUX.2: 4 axes t, h, w, l);
+ * axes_dim: host array of n_axes even dimensions (FLUX.2: 32, 32, 32, 32);
+ * out cos/sin: [n, sum(axes_dim)/2] f32. ids/cos/sin are device pointers.
+ * Reference: Flux2PosEmbed
  * (Sources/ImarelloDiT/PosEmbed.swift:12-47), Flux2RoPE.frequencies
  * (Sources/ImarelloCore/Flux2RoPE.swift:16-63). */
 int aex_rope_tables(aex_ctx* ctx, const float* ids, int n, float theta, const int* axes_dim, int n_axes,
