@@ -85,6 +85,7 @@ _SIGNATURES = [
     ("aex_joint_attention", C.c_int, [_VP, C.POINTER(aex_attention_args), _VP]),
     ("aex_joint_attention_scratch_bytes", C.c_size_t, [C.POINTER(aex_attention_args)]),
     ("aex_joint_attention_ws", C.c_int, [_VP, C.POINTER(aex_attention_args), _VP, C.c_size_t, _VP]),
+    ("aex_joint_attention_noalloc", C.c_int, [_VP, C.POINTER(aex_attention_args), _VP]),
     ("aex_rope_tables", C.c_int, [_VP, _VP, C.c_int, C.c_float, _VP, C.c_int, _VP, _VP, _VP]),
     ("aex_dequantize_mlx", C.c_int, [_VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int, _VP, _VP]),
     ("aex_qweight_create", C.c_int,

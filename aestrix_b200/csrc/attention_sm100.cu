@@ -33,6 +33,7 @@
 //    output row pitch that is a multiple of 16 bytes works (e.g. the 12288-wide
 //    concat buffer of the single-stream block).
 #include <cmath>
+#include <mutex>
 
 #include "internal.h"
 #include "sm100.cuh"
@@ -684,3 +685,62 @@ int aex_joint_attention(aex_ctx* ctx, const aex_attention_args* args, aex_stream
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-alloc
+// aex_joint_attention_noalloc: the same fused attention for callers that must
+// not allocate device memory. Some callers cannot call cudaMalloc: a host
+// framework that owns the whole device memory pool (the reference's engines
+// size one static placement heap up front, DirectDiTStep.swift:155-274, and an
+// embedding of this library may be held to the same rule), or a latency-bound
+// caller for whom cudaMalloc's implicit device-wide synchronisation would stall
+// every other stream. This entry point therefore uses a fixed scratch array
+// compiled into the library instead of context scratch.
+namespace aex {
+namespace {
+
+// 64 MiB of device memory, held by every GPU that loads the library until the
+// process exits. It covers the normalized Q and K of batch*heads*seq <= 131072
+// rows (2 * rows * 128 * 2 bytes), e.g. the 1024^2 call (1 * 24 * 4608 rows).
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device ordinal, resolved once with
+// that device current (host code must not pass the host-side symbol itself).
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+int noalloc_scratch(aex_ctx* ctx, void** out) {
+  if (ctx->device < 0 || ctx->device >= kMaxDevices)
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "device ordinal %d beyond %d", ctx->device, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[ctx->device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_error(ctx, e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_addr[ctx->device] = p;
+  }
+  *out = g_noalloc_addr[ctx->device];
+  return AEX_OK;
+}
+
+}  // namespace
+}  // namespace aex
+
+extern "C" int aex_joint_attention_noalloc(aex_ctx* ctx, const aex_attention_args* args, aex_stream stream) {
+  using namespace aex;
+  if (!ctx) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL ctx");
+  if (int r = validate(ctx, args)) return r;
+  const size_t need = aex_joint_attention_scratch_bytes(args);
+  if (need > kNoAllocScratchBytes)
+    return set_error(ctx, AEX_ERR_INVALID_ARG,
+                     "aex_joint_attention_noalloc: these args need %zu bytes of scratch (2*batch*heads*seq*256), "
+                     "above its fixed %zu-byte array (batch*heads*seq <= %zu); use aex_joint_attention or "
+                     "aex_joint_attention_ws",
+                     need, kNoAllocScratchBytes, kNoAllocScratchBytes / 512);
+  if (int r = bind_device(ctx)) return r;
+  void* ws = nullptr;
+  if (need > 0)
+    if (int r = noalloc_scratch(ctx, &ws)) return r;
+  return joint_attention_impl(ctx, args, ws, need, static_cast<cudaStream_t>(stream));
+}

@@ -130,6 +130,23 @@ size_t aex_joint_attention_scratch_bytes(const aex_attention_args* args);
 int aex_joint_attention_ws(aex_ctx* ctx, const aex_attention_args* args, void* scratch, size_t scratch_bytes,
                            aex_stream stream);
 
+/* Fused attention that allocates nothing, for callers that cannot call
+ * cudaMalloc (for example an embedding whose host framework owns the whole
+ * device memory pool, or a latency-bound caller that cannot accept
+ * cudaMalloc's implicit device-wide synchronisation). No counterpart in the
+ * reference. Same computation and arguments as aex_joint_attention, but the
+ * normalized Q/K go to a fixed scratch array compiled into the library:
+ * 64 MiB, held on every GPU that loads the library until the process exits,
+ * enough for
+ * batch*heads*seq <= 131072 (the 1024^2 call uses 110592). Larger args are
+ * rejected with AEX_ERR_INVALID_ARG. The first call on a device resolves the
+ * array's device address (cudaGetSymbolAddress) with that device current; make
+ * that first call before any stream capture. Every call shares the one array:
+ * calls whose executions overlap on the GPU (different streams or contexts of
+ * the same device) race on it. Each call fully rewrites the part it reads, so
+ * no state from an earlier call leaks into a result. */
+int aex_joint_attention_noalloc(aex_ctx* ctx, const aex_attention_args* args, aex_stream stream);
+
 /* Rotary tables. ids: [n, n_axes] f32 positions (FLUX.2: 4 axes t, h, w, l);
  * axes_dim: host array of n_axes even dimensions (FLUX.2: 32, 32, 32, 32);
  * out cos/sin: [n, sum(axes_dim)/2] f32. ids/cos/sin are device pointers.

@@ -1,0 +1,69 @@
+"""aex_joint_attention_noalloc: the fused attention entry point that allocates
+no device memory, for callers that cannot call cudaMalloc (an embedding whose
+host framework owns the whole device memory pool, or a latency-bound caller
+that cannot accept cudaMalloc's device-wide synchronisation). Its scratch is a
+fixed 64 MiB array inside the library.
+
+Checked through the C ABI against the allocating entry point aex_joint_attention
+on two calls in a row (different inputs and shapes, so the second call runs on
+scratch still holding the first call's data), with the attention tolerance of
+the other tests: relative L2 <= 1e-2 and max-abs <= 2e-2. This file is named to
+be collected last, so a run that stops at the first failure has already run
+every other test.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from aestrix_b200 import _lib, attention
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2
+ABS_TOL = 2e-2
+
+
+def _case(seed, b, s, h):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(b, s, h, 128, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    wq = (1 + 0.1 * torch.randn(128, generator=g)).float().cuda()
+    wk = (1 + 0.1 * torch.randn(128, generator=g)).float().cuda()
+    theta = torch.rand(s, 64, generator=g) * 6.2831853
+    return q, k, v, wq, wk, torch.cos(theta).cuda(), torch.sin(theta).cuda()
+
+
+def _call(ctx, fn, case, out):
+    q, k, v, wq, wk, cos, sin = case
+    a = attention.make_args(q, k, v, out, "bshd", wq, wk, 1e-5, cos, sin)
+    ctx.check(fn(ctx.handle, C.byref(a), torch.cuda.current_stream().cuda_stream))
+
+
+def test_noalloc_matches_allocating_entry_point_twice(cuda_ctx):
+    L = _lib.lib()
+    cases = [_case(901, 1, 4608, 24), _case(902, 2, 700, 8)]  # the 1024^2 call, then a ragged batched one
+    outs_na = [torch.empty_like(c[0]) for c in cases]
+    for c, o in zip(cases, outs_na):  # two no-alloc calls in a row
+        _call(cuda_ctx, L.aex_joint_attention_noalloc, c, o)
+    cuda_ctx.sync()
+    for c, o_na in zip(cases, outs_na):
+        o_ref = torch.empty_like(c[0])
+        _call(cuda_ctx, L.aex_joint_attention, c, o_ref)
+        cuda_ctx.sync()
+        got, ref = o_na.float().cpu().numpy(), o_ref.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+        mx = float(np.abs(got - ref).max())
+        assert rel <= REL_TOL and mx <= ABS_TOL, f"rel-L2 {rel:.3e} max-abs {mx:.3e}"
+    assert cuda_ctx.device_status() == 0
+
+
+def test_noalloc_rejects_args_beyond_its_scratch(cuda_ctx):
+    q, k, v, wq, wk, cos, sin = _case(903, 1, 64, 4)
+    out = torch.empty_like(q)
+    a = attention.make_args(q, k, v, out, "bshd", wq, wk, 1e-5, cos, sin)
+    a.batch, a.seq, a.heads = 2, 4608, 24  # 221184 rows > 131072: rejected before any launch
+    rc = _lib.lib().aex_joint_attention_noalloc(cuda_ctx.handle, C.byref(a), None)
+    assert rc == _lib.AEX_ERR_INVALID_ARG
+    assert b"fixed" in _lib.lib().aex_last_error_string(cuda_ctx.handle)
