@@ -22,12 +22,12 @@ struct aex_ctx {
 };
 
 struct aex_qweight {
+  int device = 0;
   int n = 0, k = 0, group_size = 64;
-  int n_tiles = 0;             // ceil(n / kQTileN)
-  uint8_t* packed = nullptr;   // tile layout, see qmm_sm100.cu
-  float* scale = nullptr;      // [n_tiles*kQTileN, k/64] f32 (zero for padded rows)
-  float* bias = nullptr;       // same shape
-  size_t packed_bytes = 0;
+  int n_tiles = 0;          // ceil(n / 256)
+  int k_blocks = 0;         // k / 64
+  uint8_t* tiles = nullptr; // tile layout (qmm_sm100.cu): one 9 KB chunk per (256-row tile, 64-wide K block)
+  size_t bytes = 0;
 };
 
 namespace aex {
