@@ -466,31 +466,49 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
   const int half = lane >> 4;  // which row of the pair
   const int l16 = lane & 15;   // 8-element slice of the row
   const uint32_t warp_row0 = (blockIdx.x * kPrepWarps + (threadIdx.x >> 5)) * kPrepRowsPerWarp;
-  uint4 raw[kPrepRowsPerWarp / 2];
+  constexpr int kIt = kPrepRowsPerWarp / 2;
+  // Issue every global load of this thread first (row slices, rotary tables,
+  // norm weights), so their latencies overlap; then compute and store.
+  uint4 raw[kIt];
+  float4 cs[kIt], sn[kIt];
+  int64_t dst_off[kIt];
+  bool valid[kIt];
+  uint32_t which_of[kIt];
 #pragma unroll
-  for (int it = 0; it < kPrepRowsPerWarp / 2; ++it) {
+  for (int it = 0; it < kIt; ++it) {
     const uint32_t row = warp_row0 + 2 * it + half;
-    raw[it] = make_uint4(0, 0, 0, 0);
-    if (row < total) {
-      const uint32_t which = row >= rows_per_op ? 1 : 0;
-      const uint32_t r = row - which * rows_per_op;
-      const int64_t hh = r % heads;
-      const int64_t s = (r / heads) % seq;
-      const int64_t bb = r / (heads * seq);
-      const __nv_bfloat16* src = which ? p.k + bb * p.k_sb + s * p.k_ss + hh * p.k_sh
-                                       : p.q + bb * p.q_sb + s * p.q_ss + hh * p.q_sh;
-      raw[it] = __ldg(reinterpret_cast<const uint4*>(src) + l16);
-    }
-  }
-#pragma unroll
-  for (int it = 0; it < kPrepRowsPerWarp / 2; ++it) {
-    const uint32_t row = warp_row0 + 2 * it + half;
-    const bool valid = row < total;
-    const uint32_t which = row >= rows_per_op ? 1 : 0;
-    const uint32_t r = row - which * rows_per_op;
+    valid[it] = row < total;
+    const uint32_t rr = valid[it] ? row : 0;
+    const uint32_t which = rr >= rows_per_op ? 1 : 0;
+    const uint32_t r = rr - which * rows_per_op;
     const int64_t hh = r % heads;
     const int64_t s = (r / heads) % seq;
     const int64_t bb = r / (heads * seq);
+    which_of[it] = which;
+    const __nv_bfloat16* src = which ? p.k + bb * p.k_sb + s * p.k_ss + hh * p.k_sh
+                                     : p.q + bb * p.q_sb + s * p.q_ss + hh * p.q_sh;
+    raw[it] = valid[it] ? __ldg(reinterpret_cast<const uint4*>(src) + l16) : make_uint4(0, 0, 0, 0);
+    if (p.cos_t) {
+      cs[it] = __ldg(reinterpret_cast<const float4*>(p.cos_t + s * (kD / 2) + l16 * 4));
+      sn[it] = __ldg(reinterpret_cast<const float4*>(p.sin_t + s * (kD / 2) + l16 * 4));
+    }
+    dst_off[it] = static_cast<int64_t>(which) * rows_per_op * kD + ((bb * heads + hh) * seq + s) * kD + l16 * 8;
+  }
+  float wq[8], wk[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) wq[i] = wk[i] = 1.f;
+  if (p.wq) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p.wq + l16 * 8));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p.wq + l16 * 8 + 4));
+    wq[0] = a.x; wq[1] = a.y; wq[2] = a.z; wq[3] = a.w; wq[4] = b.x; wq[5] = b.y; wq[6] = b.z; wq[7] = b.w;
+  }
+  if (p.wk) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p.wk + l16 * 8));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p.wk + l16 * 8 + 4));
+    wk[0] = a.x; wk[1] = a.y; wk[2] = a.z; wk[3] = a.w; wk[4] = b.x; wk[5] = b.y; wk[6] = b.z; wk[7] = b.w;
+  }
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
     float x[8];
     const uint32_t wv4[4] = {raw[it].x, raw[it].y, raw[it].z, raw[it].w};
 #pragma unroll
@@ -498,26 +516,22 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
       x[2 * i] = bf16lo_to_f32(wv4[i]);
       x[2 * i + 1] = bf16hi_to_f32(wv4[i]);
     }
-    const float* w = which ? p.wk : p.wq;
     // The two half-warps may hold rows of different operands (Q and K), so the
-    // reduction runs for every lane and only its use depends on `w`.
+    // reduction runs for every lane and only its use depends on the operand.
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (w) {
+    const bool normed = which_of[it] ? (p.wk != nullptr) : (p.wq != nullptr);
+    if (normed) {
       const float inv = rsqrtf(ss * (1.0f / kD) + p.eps);
-      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + l16 * 8));
-      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + l16 * 8 + 4));
-      const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * wa[i];
+      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * (which_of[it] ? wk[i] : wq[i]);
     }
-    if (p.cos_t && valid) {
-      const float4 c = __ldg(reinterpret_cast<const float4*>(p.cos_t + s * (kD / 2) + l16 * 4));
-      const float4 sn = __ldg(reinterpret_cast<const float4*>(p.sin_t + s * (kD / 2) + l16 * 4));
-      const float ca[4] = {c.x, c.y, c.z, c.w}, sa[4] = {sn.x, sn.y, sn.z, sn.w};
+    if (p.cos_t) {
+      const float ca[4] = {cs[it].x, cs[it].y, cs[it].z, cs[it].w};
+      const float sa[4] = {sn[it].x, sn[it].y, sn[it].z, sn[it].w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float re = x[2 * i], im = x[2 * i + 1];
@@ -525,12 +539,9 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
         x[2 * i + 1] = im * ca[i] + re * sa[i];
       }
     }
-    if (valid) {
-      __nv_bfloat16* dst = p.out + static_cast<int64_t>(which) * rows_per_op * kD +
-                           ((bb * heads + hh) * seq + s) * kD + l16 * 8;
-      *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
-                                                  pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
-    }
+    if (valid[it])
+      *reinterpret_cast<uint4*>(p.out + dst_off[it]) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                                                                   pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
   }
 }
 

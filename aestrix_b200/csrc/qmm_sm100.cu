@@ -19,7 +19,7 @@
 //     One bulk copy moves one chunk into shared memory.
 // K2  gemm_kernel<MT> — tcgen05 GEMM, CTA tile (128*MT) x 256 x 64-wide K steps:
 //     warp 0 TMA producer (x tile) + bulk copy (packed chunk), warp 1 UMMA
-//     issuer, warps 4..11 dequantize the chunk in registers into the 128-byte
+//     issuer, warps 4..19 dequantize the chunk in registers into the 128-byte
 //     swizzled K-major bf16 B tile and, after the main loop, drain the f32
 //     accumulators from tensor memory (epilogue).
 //     gemv_kernel<R> — R <= 16 activation rows, HBM-bound: one thread per
@@ -121,9 +121,9 @@ __global__ void __launch_bounds__(256) dequant_mlx_kernel(const uint32_t* __rest
 }
 
 // ------------------------------------------------------------------ K2 GEMM
-constexpr int kGemmThreads = 384;  // warps 0 producer, 1 UMMA, 2-3 idle, 4-11 dequant + epilogue
+constexpr int kGemmThreads = 640;  // warps 0 producer, 1 UMMA, 2-3 idle, 4-19 dequant + epilogue
 constexpr int kDequantWarp0 = 4;
-constexpr int kDequantThreads = 256;
+constexpr int kDequantThreads = 512;  // one half-row (4 packed words, 32 codes) per thread per K block
 constexpr int kGemmStages = 3;
 constexpr uint32_t kIdescGemm = idesc_bf16_f32(128, 256, false, false);
 
@@ -251,15 +251,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
       const uint8_t* pk = smem + s * L::kStageBytes + L::kOffPk;
       uint8_t* bt = smem + s * L::kStageBytes + L::kOffB;
-#pragma unroll 2
-      for (int i = 0; i < 8; ++i) {
-        const int wi = dt + kDequantThreads * i;  // word: row wi/8, column chunk wi%8
-        const int row = wi >> 3, c = wi & 7;
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(pk + row * 32 + c * 4);
+      {
+        const int row = dt >> 1, hw = dt & 1;  // row of the B tile, half (words 4*hw .. 4*hw+3)
+        const uint4 w4 = *reinterpret_cast<const uint4*>(pk + row * 32 + hw * 16);
         const float sc = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(pk + kOffScale)[row]);
         const float bi = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(pk + kOffBias)[row]);
-        *reinterpret_cast<uint4*>(bt + (row >> 3) * 1024 + (row & 7) * 128 + ((c ^ (row & 7)) << 4)) =
-            dequant_word(w, sc, bi);
+        uint8_t* brow = bt + (row >> 3) * 1024 + (row & 7) * 128;
+        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = hw * 4 + i;
+          *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = dequant_word(ws[i], sc, bi);
+        }
       }
       fence_async_shared();  // generic-proxy stores -> visible to the tensor core
       __syncwarp();
@@ -271,14 +274,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (ok) {
       tc_fence_after();
       const int quad = warp & 3;
-      const int half = (warp - kDequantWarp0) >> 2;  // columns [128*half, +128)
-      const int n0 = nt * kTileN + half * 128;
+      const int quarter = (warp - kDequantWarp0) >> 2;  // columns [64*quarter, +64)
+      const int n0 = nt * kTileN + quarter * 64;
 #pragma unroll 1
       for (int mt = 0; mt < MT; ++mt) {
         const int row = m0 + mt * 128 + quad * 32 + lane;
-        const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + mt * 256 + half * 128;
+        const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + mt * 256 + quarter * 64;
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
+        for (int c0 = 0; c0 < 64; c0 += 32) {
           uint32_t r[32];
           tmem_ld32(tbase + c0, r);
           tmem_wait_ld();
@@ -327,6 +330,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ------------------------------------------------------------------ GEMV
 constexpr int kGemvRows = 128;     // weight rows (outputs) per CTA, one per thread
 constexpr int kGemvMaxSplit = 8;   // cluster size along K (portable limit)
+constexpr int kGemvMaxKbps = 8;    // K blocks per CTA (weights prefetched into registers)
 
 struct GemvParams {
   const uint16_t* x;  // bf16 [m, ldx]
@@ -370,14 +374,27 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
 #pragma unroll
   for (int mr = 0; mr < R; ++mr) acc[mr] = 0.f;
   if (row < p.n) {
-#pragma unroll 2
-    for (int g = 0; g < nkb; ++g) {
-      const uint8_t* chunk = p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks);
-      const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32));
-      const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32) + 1);
-      const float sc = bf16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(chunk + kOffScale) + r));
-      const float bi = bf16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(chunk + kOffBias) + r));
-      const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    // Issue every weight load of this thread's K range first (kGemvMaxKbps
+    // blocks of 32 packed bytes + scale + bias), then consume them.
+    uint4 wv[2 * kGemvMaxKbps];
+    uint16_t sv[kGemvMaxKbps], bv[kGemvMaxKbps];
+#pragma unroll
+    for (int g = 0; g < kGemvMaxKbps; ++g) {
+      if (g < nkb) {
+        const uint8_t* chunk = p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks);
+        wv[2 * g] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32));
+        wv[2 * g + 1] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32) + 1);
+        sv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffScale) + r);
+        bv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffBias) + r);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kGemvMaxKbps; ++g) {
+      if (g >= nkb) break;
+      const float sc = bf16_bits_to_f32(sv[g]);
+      const float bi = bf16_bits_to_f32(bv[g]);
+      const uint32_t ws[8] = {wv[2 * g].x, wv[2 * g].y, wv[2 * g].z, wv[2 * g].w,
+                              wv[2 * g + 1].x, wv[2 * g + 1].y, wv[2 * g + 1].z, wv[2 * g + 1].w};
       float2 tq[R];
 #pragma unroll
       for (int mr = 0; mr < R; ++mr) tq[mr] = make_float2(0.f, 0.f);
@@ -462,16 +479,17 @@ template <int R>
 int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
                 int y_f32, cudaStream_t s) {
   const int n_ctas = (w->n + qmm::kGemvRows - 1) / qmm::kGemvRows;
-  int split = std::max(1, std::min(qmm::kGemvMaxSplit, (2 * ctx->sm_count + n_ctas - 1) / n_ctas));
+  // Enough CTAs to cover every SM several times, and at most kGemvMaxKbps K blocks per CTA.
+  int split = std::max(1, std::min(qmm::kGemvMaxSplit, (4 * ctx->sm_count + n_ctas - 1) / n_ctas));
+  split = std::max(split, (w->k_blocks + qmm::kGemvMaxKbps - 1) / qmm::kGemvMaxKbps);
+  if (split > qmm::kGemvMaxSplit)
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d needs more than %d K splits", w->k,
+                     qmm::kGemvMaxSplit);
   split = std::min(split, w->k_blocks);
   int kbps = (w->k_blocks + split - 1) / split;
   // x slice + group sums + partials in dynamic shared memory (<= 200 KB).
   auto smem_for = [&](int kb) { return static_cast<size_t>(R) * (kb * 64 + kb + qmm::kGemvRows) * 4; };
   constexpr size_t kMaxSmem = 200 * 1024;
-  while (smem_for(kbps) > kMaxSmem && split < qmm::kGemvMaxSplit) {
-    ++split;
-    kbps = (w->k_blocks + split - 1) / split;
-  }
   if (smem_for(kbps) > kMaxSmem)
     return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w->k, R);
   split = (w->k_blocks + kbps - 1) / kbps;
@@ -586,7 +604,7 @@ int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int 
   if (int r = bind_device(ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
   const int f32 = y_dtype == AEX_DTYPE_F32;
-  if (m <= 16) {
+  if (m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps) {
     if (m <= 1) return launch_gemv<1>(ctx, w, x, ldx, m, y, ldy, f32, s);
     if (m <= 2) return launch_gemv<2>(ctx, w, x, ldx, m, y, ldy, f32, s);
     if (m <= 4) return launch_gemv<4>(ctx, w, x, ldx, m, y, ldy, f32, s);

@@ -62,6 +62,14 @@ def _peaks():
         return 1590.0, "fallback"
 
 
+def _hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except Exception:
+        return 6650.0
+
+
 def _rope_tables():
     """Text positions 0, image ids (0, h, w, 0) on the 64x64 grid (Flux2RoPE.prepareGridIDs)."""
     ids = np.zeros((SEQ, 4), np.float32)
@@ -251,6 +259,44 @@ def run_reference(args):
     return 0
 
 
+def measure_qmm(ctx, dev, iters=20):
+    """4-bit affine linears 3072 -> 9216 (QKV) and 3072 -> 18432 (SwiGLU) at
+    M in {4608, 512, 1}. Weights rotate over enough device copies to exceed L2 (> 160 MB), so every
+    call streams its weight from HBM. TFLOP/s = 2*M*N*K / time; GB/s = algorithmic bytes
+    (N*K/2 packed + N*K/64*4 bf16 scale+bias + 2*M*K x + 2*M*N y) / time."""
+    import torch
+
+    from aestrix_b200 import qmm
+
+    K = 3072
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    for N in (9216, 18432):
+        packed, scales, biases = qmm.synthetic_weight(N, K, seed=N)
+        wbytes = N * K // 2 + N * (K // 64) * 4
+        copies = max(2, math.ceil(160e6 / wbytes))
+        ws = [qmm.QuantizedWeight(packed.clone(), scales.clone(), biases.clone(), ctx=ctx) for _ in range(copies)]
+        for M in (4608, 512, 1):
+            x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).to(torch.bfloat16).to(dev)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            for i in range(3):
+                ws[i % copies](x, out=y, stream=stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(iters):
+                ws[i % copies](x, out=y, stream=stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            nbytes = wbytes + 2 * M * K + 2 * M * N
+            out[f"M{M}_N{N}"] = {"ms": ms, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
+                                 "gbs": nbytes / (ms * 1e-3) / 1e9,
+                                 "kernel": "gemv_kernel" if M <= 16 else "gemm_kernel",
+                                 "bound": "hbm" if M <= 16 else "tensor"}
+        del ws
+    return out
+
+
 def run_ours(args):
     import torch
 
@@ -346,6 +392,7 @@ def run_ours(args):
     e2e_ms = _max_over_ranks(world, ea.elapsed_time(eb) / n_e)
     _barrier(world)
 
+    qmm_res = measure_qmm(ctx, dev) if not args.no_qmm else None
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = FLOPS_PER_CALL / (kernel_ms * 1e-3) / 1e12
@@ -368,6 +415,12 @@ def run_ours(args):
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
+        if qmm_res is not None:
+            hbm = _hbm_peak()
+            for v in qmm_res.values():
+                v["frac"] = v["gbs"] / hbm if v["bound"] == "hbm" else v["tflops"] / peak
+            line["qmm"] = dict(qmm_res, note="BASELINE configs[2], K=3072; frac of measured HBM GB/s (M=1) or "
+                               "measured bf16 TF/s (M>=512)")
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -384,6 +437,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=SEQ, help="query rows in the CPU-baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target duration of the reference arm")
+    ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
