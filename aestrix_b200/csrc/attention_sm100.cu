@@ -286,8 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      ok = mbar_wait_addr(bar_s, j & 1, &abort_flag, status, kDevTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = mbar_wait_warp_addr(bar_s, j & 1, &abort_flag, status, kDevTimeoutSoftmax);
       if (!ok) break;
       tc_fence_after();
       uint32_t r[128];
@@ -392,8 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_addr(bar_p + 8);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok) ok = mbar_wait(&bars[kBarOFull + t], 0, &abort_flag, status, kDevTimeoutEpilogue);
-    ok = __all_sync(0xffffffffu, ok);
+    if (ok) ok = mbar_wait_warp(&bars[kBarOFull + t], 0, &abort_flag, status, kDevTimeoutEpilogue);
     uint8_t* stage = smem + kOffQ + t * kTileBytes;  // Q_t is dead once O_t is final
     if (ok) {
       tc_fence_after();

@@ -246,8 +246,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     bool ok = true;
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % kGemmStages, use = kb / kGemmStages;
-      ok = mbar_wait(&full[s], use & 1, &abort_flag, status, kDevTimeoutProducer);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = mbar_wait_warp(&full[s], use & 1, &abort_flag, status, kDevTimeoutProducer);
       if (!ok) break;
       const uint8_t* pk = smem + s * L::kStageBytes + L::kOffPk;
       uint8_t* bt = smem + s * L::kStageBytes + L::kOffB;
@@ -269,8 +268,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive(&bready[s]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok) ok = mbar_wait(acc, 0, &abort_flag, status, kDevTimeoutEpilogue);
-    ok = __all_sync(0xffffffffu, ok);
+    if (ok) ok = mbar_wait_warp(acc, 0, &abort_flag, status, kDevTimeoutEpilogue);
     if (ok) {
       tc_fence_after();
       const int quad = warp & 3;
@@ -354,40 +352,49 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   const int kb0 = split * kbps;
   const int kb1 = min(p.k_blocks, kb0 + kbps);
   const int nkb = max(0, kb1 - kb0);
-  // Stage this split's x slice as f32 and its per-group sums.
+  const int row = blockIdx.x * kGemvRows + t;  // weight row (output column)
+  const int nt = row / kTileN, r = row % kTileN;
+  const bool active = row < p.n;
+  // 1. Issue every weight load of this thread's K range (kGemvMaxKbps blocks
+  //    of 32 packed bytes + scale + bias) before anything else, so the HBM
+  //    fetch overlaps the x staging below.
+  uint4 wv[2 * kGemvMaxKbps];
+  uint16_t sv[kGemvMaxKbps], bv[kGemvMaxKbps];
+#pragma unroll
+  for (int g = 0; g < kGemvMaxKbps; ++g) {
+    if (active && g < nkb) {
+      const uint8_t* chunk = p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks);
+      wv[2 * g] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32));
+      wv[2 * g + 1] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32) + 1);
+      sv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffScale) + r);
+      bv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffBias) + r);
+    }
+  }
+  // 2. Stage this split's x slice as f32, then per-group sums (one warp per
+  //    (row, group) pair, shuffle-reduced).
   for (int i = t; i < R * nkb * kKB; i += kGemvRows) {
     const int mr = i / (nkb * kKB), kk = i % (nkb * kKB);
     xs[mr * kbps * kKB + kk] =
         mr < p.m ? bf16_bits_to_f32(p.x[static_cast<int64_t>(mr) * p.ldx + kb0 * kKB + kk]) : 0.f;
   }
   __syncthreads();
-  for (int i = t; i < R * nkb; i += kGemvRows) {
-    const int mr = i / nkb, g = i % nkb;
-    float s = 0.f;
-    for (int kk = 0; kk < kKB; ++kk) s += xs[mr * kbps * kKB + g * kKB + kk];
-    gsum[mr * kbps + g] = s;
+  {
+    const int warp = t >> 5, lane = t & 31;
+    for (int i = warp; i < R * nkb; i += kGemvRows / 32) {
+      const int mr = i / nkb, g = i % nkb;
+      const float* xg = xs + mr * kbps * kKB + g * kKB;
+      float s = xg[lane] + xg[lane + 32];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) gsum[mr * kbps + g] = s;
+    }
   }
   __syncthreads();
-  const int row = blockIdx.x * kGemvRows + t;  // weight row (output column)
-  const int nt = row / kTileN, r = row % kTileN;
+  // 3. Dot products: y_m += scale * sum_k(x_mk * q_k) + bias * sum_k(x_mk) per group.
   float acc[R];
 #pragma unroll
   for (int mr = 0; mr < R; ++mr) acc[mr] = 0.f;
-  if (row < p.n) {
-    // Issue every weight load of this thread's K range first (kGemvMaxKbps
-    // blocks of 32 packed bytes + scale + bias), then consume them.
-    uint4 wv[2 * kGemvMaxKbps];
-    uint16_t sv[kGemvMaxKbps], bv[kGemvMaxKbps];
-#pragma unroll
-    for (int g = 0; g < kGemvMaxKbps; ++g) {
-      if (g < nkb) {
-        const uint8_t* chunk = p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks);
-        wv[2 * g] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32));
-        wv[2 * g + 1] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32) + 1);
-        sv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffScale) + r);
-        bv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffBias) + r);
-      }
-    }
+  if (active) {
 #pragma unroll
     for (int g = 0; g < kGemvMaxKbps; ++g) {
       if (g >= nkb) break;
@@ -419,9 +426,9 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   }
 #pragma unroll
   for (int mr = 0; mr < R; ++mr) part[mr * kGemvRows + t] = acc[mr];
-  // Reduce the K splits of this cluster in CTA rank 0 through distributed shared memory.
+  // 4. Reduce the K splits of this cluster in CTA rank 0 through distributed shared memory.
   cluster_sync_all();
-  if (cluster_ctarank() == 0 && row < p.n) {
+  if (cluster_ctarank() == 0 && active) {
     const uint32_t my_part = smem_u32(part);
     for (int mr = 0; mr < R && mr < p.m; ++mr) {
       float v = 0.f;

@@ -103,7 +103,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// Same as above on a 32-bit shared-window address (keeps hot loops lean).
+// Warp-wide bounded wait, returning the same result in every lane; must be
+// called by all 32 lanes. By default every lane waits (threads suspended in
+// try_wait are woken by the phase flip); AEX_WAIT_LANE0 makes lane 0 poll
+// alone and the warp synchronize afterwards (measured slower on B200).
+#ifndef AEX_WAIT_LANE0
+#define AEX_WAIT_LANE0 0
+#endif
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                               int code) {
+  if (AEX_WAIT_LANE0) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+  }
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, code));
+}
+
+// Same as mbar_wait on a 32-bit shared-window address (keeps hot loops lean).
 __device__ __forceinline__ bool mbar_wait_addr(uint32_t a, uint32_t parity, volatile int* abort_flag, int* status,
                                                int code) {
   if (mbar_try_wait(a, parity)) return true;
@@ -119,6 +138,18 @@ __device__ __forceinline__ bool mbar_wait_addr(uint32_t a, uint32_t parity, vola
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait_warp_addr(uint32_t a, uint32_t parity, volatile int* abort_flag,
+                                                    int* status, int code) {
+  if (AEX_WAIT_LANE0) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait_addr(a, parity, abort_flag, status, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+  }
+  return __all_sync(0xffffffffu, mbar_wait_addr(a, parity, abort_flag, status, code));
 }
 
 __device__ __forceinline__ void mbar_arrive_addr(uint32_t a) {
