@@ -72,6 +72,12 @@ class aex_attention_args(C.Structure):
     ]
 
 
+class aex_dit_config(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "heads", "n_double", "n_single", "mlp_hidden", "in_channels",
+                                       "text_dim", "timestep_dim", "l_txt", "l_img")] + [
+        ("rms_eps", C.c_float), ("ln_eps", C.c_float)]
+
+
 # (name, restype, argtypes) for every symbol declared in include/aestrix_cuda.h.
 _VP = C.c_void_p
 _SIGNATURES = [
@@ -94,6 +100,16 @@ _SIGNATURES = [
     ("aex_qweight_shape", C.c_int, [_VP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     ("aex_qweight_dequantize", C.c_int, [_VP, _VP, _VP, _VP]),
     ("aex_qmm", C.c_int, [_VP, _VP, _VP, C.c_int64, C.c_int, _VP, C.c_int64, C.c_int, _VP]),
+    ("aex_dit_create", C.c_int, [_VP, C.POINTER(aex_dit_config), C.POINTER(_VP)]),
+    ("aex_dit_destroy", None, [_VP]),
+    ("aex_dit_load_linear", C.c_int, [_VP, C.c_char_p, _VP, _VP, _VP, C.c_int, C.c_int, _VP]),
+    ("aex_dit_load_norm", C.c_int, [_VP, C.c_char_p, _VP, _VP]),
+    ("aex_dit_set_rope", C.c_int, [_VP, _VP, _VP, _VP]),
+    ("aex_dit_project_context", C.c_int, [_VP, _VP, _VP]),
+    ("aex_dit_set_timestep", C.c_int, [_VP, C.c_float, _VP]),
+    ("aex_dit_forward", C.c_int, [_VP, _VP, _VP, _VP]),
+    ("aex_dit_denoise_step", C.c_int, [_VP, _VP, _VP, C.c_float, _VP]),
+    ("aex_dit_denoise", C.c_int, [_VP, _VP, C.c_int, _VP]),
     ("aex_selftest_umma", C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
 ]
 

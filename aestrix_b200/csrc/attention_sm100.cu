@@ -440,8 +440,14 @@ struct PrepParams {
   const __nv_bfloat16* k;
   int64_t q_sb, q_ss, q_sh;
   int64_t k_sb, k_ss, k_sh;
+  // Norm weights per row segment: tokens s < split use (wq_a, wk_a), the rest
+  // (wq, wk). The double-stream block norms its text rows with norm_added_q/k
+  // and its image rows with norm_q/k (JointAttention.swift:61-83).
   const float* wq;
   const float* wk;
+  const float* wq_a;
+  const float* wk_a;
+  int split;
   const float* cos_t;
   const float* sin_t;
   float eps;
@@ -472,6 +478,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
   int64_t dst_off[kIt];
   bool valid[kIt];
   uint32_t which_of[kIt];
+  bool seg_a[kIt];
 #pragma unroll
   for (int it = 0; it < kIt; ++it) {
     const uint32_t row = warp_row0 + 2 * it + half;
@@ -483,6 +490,7 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
     const int64_t s = (r / heads) % seq;
     const int64_t bb = r / (heads * seq);
     which_of[it] = which;
+    seg_a[it] = s < p.split;
     const __nv_bfloat16* src = which ? p.k + bb * p.k_sb + s * p.k_ss + hh * p.k_sh
                                      : p.q + bb * p.q_sb + s * p.q_ss + hh * p.q_sh;
     raw[it] = valid[it] ? __ldg(reinterpret_cast<const uint4*>(src) + l16) : make_uint4(0, 0, 0, 0);
@@ -492,19 +500,13 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
     }
     dst_off[it] = static_cast<int64_t>(which) * rows_per_op * kD + ((bb * heads + hh) * seq + s) * kD + l16 * 8;
   }
-  float wq[8], wk[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) wq[i] = wk[i] = 1.f;
-  if (p.wq) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p.wq + l16 * 8));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(p.wq + l16 * 8 + 4));
-    wq[0] = a.x; wq[1] = a.y; wq[2] = a.z; wq[3] = a.w; wq[4] = b.x; wq[5] = b.y; wq[6] = b.z; wq[7] = b.w;
-  }
-  if (p.wk) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p.wk + l16 * 8));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(p.wk + l16 * 8 + 4));
-    wk[0] = a.x; wk[1] = a.y; wk[2] = a.z; wk[3] = a.w; wk[4] = b.x; wk[5] = b.y; wk[6] = b.z; wk[7] = b.w;
-  }
+  auto load_w = [&](const float* w, float (&d)[8]) {
+    if (w) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(w + l16 * 8));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(w + l16 * 8 + 4));
+      d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+    }
+  };
 #pragma unroll
   for (int it = 0; it < kIt; ++it) {
     float x[8];
@@ -521,11 +523,13 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
     for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const bool normed = which_of[it] ? (p.wk != nullptr) : (p.wq != nullptr);
-    if (normed) {
+    const float* w = which_of[it] ? (seg_a[it] ? p.wk_a : p.wk) : (seg_a[it] ? p.wq_a : p.wq);
+    if (w) {
+      float wl[8];
+      load_w(w, wl);
       const float inv = rsqrtf(ss * (1.0f / kD) + p.eps);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * (which_of[it] ? wk[i] : wq[i]);
+      for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * wl[i];
     }
     if (p.cos_t) {
       const float ca[4] = {cs[it].x, cs[it].y, cs[it].z, cs[it].w};
@@ -594,6 +598,38 @@ int bshd_tmap(aex_ctx* ctx, CUtensorMap* m, const void* base, int64_t sb, int64_
 
 }  // namespace
 
+int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
+                   int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
+                   float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream) {
+  attn::PrepParams pp{};
+  pp.q = static_cast<const __nv_bfloat16*>(q);
+  pp.k = static_cast<const __nv_bfloat16*>(k);
+  pp.q_sb = qs[0];
+  pp.q_ss = qs[1];
+  pp.q_sh = qs[2];
+  pp.k_sb = ks[0];
+  pp.k_ss = ks[1];
+  pp.k_sh = ks[2];
+  pp.wq = wq;
+  pp.wk = wk;
+  pp.wq_a = wq_a;
+  pp.wk_a = wk_a;
+  pp.split = split;
+  pp.cos_t = cos_t;
+  pp.sin_t = sin_t;
+  pp.eps = eps;
+  pp.batch = B;
+  pp.seq = S;
+  pp.heads = H;
+  pp.out = static_cast<__nv_bfloat16*>(out);
+  const int64_t rows = 2ll * B * S * H;
+  const int64_t per_block = attn::kPrepWarps * attn::kPrepRowsPerWarp;
+  const int64_t blocks = (rows + per_block - 1) / per_block;
+  if (rows >= (1ll << 31)) return set_error(ctx, AEX_ERR_INVALID_ARG, "batch*seq*heads too large");
+  attn::qk_prep_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(pp);
+  return check_launch(ctx, "qk_prep_kernel");
+}
+
 int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
                          cudaStream_t stream) {
   const int B = a->batch, S = a->seq, H = a->heads;
@@ -608,30 +644,9 @@ int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratc
                        need);
     if (reinterpret_cast<uintptr_t>(scratch) % 256)
       return set_error(ctx, AEX_ERR_INVALID_ARG, "scratch must be 256-byte aligned");
-    attn::PrepParams pp{};
-    pp.q = static_cast<const __nv_bfloat16*>(a->q.data);
-    pp.k = static_cast<const __nv_bfloat16*>(a->k.data);
-    pp.q_sb = a->q.stride_b;
-    pp.q_ss = a->q.stride_s;
-    pp.q_sh = a->q.stride_h;
-    pp.k_sb = a->k.stride_b;
-    pp.k_ss = a->k.stride_s;
-    pp.k_sh = a->k.stride_h;
-    pp.wq = a->norm_q_weight;
-    pp.wk = a->norm_k_weight;
-    pp.cos_t = a->rope_cos;
-    pp.sin_t = a->rope_sin;
-    pp.eps = a->eps;
-    pp.batch = B;
-    pp.seq = S;
-    pp.heads = H;
-    pp.out = static_cast<__nv_bfloat16*>(scratch);
-    const int64_t rows = 2ll * B * S * H;
-    const int64_t per_block = attn::kPrepWarps * attn::kPrepRowsPerWarp;
-    const int64_t blocks = (rows + per_block - 1) / per_block;
-    if (rows >= (1ll << 31)) return set_error(ctx, AEX_ERR_INVALID_ARG, "batch*seq*heads too large");
-    attn::qk_prep_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(pp);
-    if (int r = check_launch(ctx, "qk_prep_kernel")) return r;
+    if (int r = launch_qk_prep(ctx, a->q.data, qs, a->k.data, ks, B, S, H, a->norm_q_weight, a->norm_k_weight,
+                               nullptr, nullptr, 0, a->eps, a->rope_cos, a->rope_sin, scratch, stream))
+      return r;
     const int64_t plane = static_cast<int64_t>(B) * H * S * 128;
     qsrc = scratch;
     ksrc = static_cast<const __nv_bfloat16*>(scratch) + plane;

@@ -1,0 +1,484 @@
+// dit_engine.cpp — the FLUX.2-klein transformer step on one B200: host-side
+// engine over the library's kernels (qmm, attention, glue).
+//
+// Mirrors the reference direct engine (Sources/ImarelloDirect/DirectDiTStep.swift)
+// and its conditioner (DirectConditioner.swift):
+//  * one static buffer plan allocated at creation (allocateScratch :155-274);
+//  * weights keyed by their MLX names (loadBlocks/loadHead :294-335, 844-884);
+//  * one f32 residual X [J, hidden] whose rows [0, l_txt) are the text stream
+//    and [l_txt, J) the image stream, so the double->single "concat" blit
+//    (encodeBlocks :662-670) disappears;
+//  * double block (encodeDouble :546-588, Flux2TransformerBlock
+//    TransformerBlock.swift:25-74): per stream LN+mod -> fused Q|K|V linear;
+//    joint QK-RMSNorm (norm_added_* on text rows, norm_* on image rows) + RoPE;
+//    attention; out-projections with the gated residual fused into the GEMM
+//    epilogue; LN+mod -> FFN in -> SwiGLU -> FFN out (gated residual fused);
+//  * single block (encodeSingle :590-618, ParallelSelfAttention.swift:30-132):
+//    LN+mod -> to_qkv_mlp_proj -> [Q|K|V|g|u]; SwiGLU into the right half of
+//    the concat buffer; attention into its left half; to_out with the gated
+//    residual fused;
+//  * head (encodeDenoiseStep :908-971): norm_out LN+mod on image rows ->
+//    proj_out -> velocity; Euler update.
+// Modulation vectors are [shift | scale | gate] per set (two sets for each
+// double stream, one for the single blocks); norm_out is [scale | shift]
+// (DirectConditioner.stepConditioning :172-213, AdaLayerNormContinuous.swift).
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "dit_internal.h"
+
+struct aex_dit {
+  aex_ctx* ctx = nullptr;
+  aex_dit_config cfg{};
+  int J = 0, C = 0, H = 0, mlp = 0, proj = 0, cat = 0;
+  std::unordered_map<std::string, aex_qweight*> lin;
+  std::unordered_map<std::string, float*> norms;
+  std::vector<void*> allocs;
+  // buffers
+  float* X = nullptr;         // [J, C] f32 residual (text rows first)
+  float* E0 = nullptr;        // [l_txt, C] f32 projected context
+  uint16_t* NH = nullptr;     // [J, C] bf16 LN+mod output
+  uint16_t* PROJ = nullptr;   // [J, max(3C + 2 mlp, 2 mlp)] bf16: Q|K|V(|g|u) or FFN-in output
+  uint16_t* ATT = nullptr;    // [J, C + mlp] bf16: attention output | SwiGLU (single); SwiGLU [rows, mlp] (double FFN)
+  uint16_t* PREP = nullptr;   // [2][H][J][128] bf16 normalized + rotated Q, K
+  float* COS = nullptr;       // [J, 64]
+  float* SIN = nullptr;
+  uint16_t* LAT16 = nullptr;  // [l_img, in_ch] bf16
+  float* PRED = nullptr;      // [l_img, in_ch] f32 velocity
+  float* LATB = nullptr;      // [l_img, in_ch] f32 Euler ping-pong
+  float* TSIN = nullptr;      // [timestep_dim]
+  uint16_t* TSIN16 = nullptr;
+  float* T1 = nullptr;        // [C]
+  uint16_t* T16 = nullptr;    // [C]
+  float* TEMB = nullptr;      // [C]
+  float* MOD_IMG = nullptr;   // [6C]
+  float* MOD_TXT = nullptr;   // [6C]
+  float* MOD_SINGLE = nullptr;  // [3C]
+  float* MOD_OUT = nullptr;   // [2C]
+  bool rope_set = false, context_set = false, timestep_set = false;
+};
+
+namespace aex {
+namespace {
+
+template <class T>
+int dalloc(aex_dit* d, T** p, size_t count) {
+  void* v = nullptr;
+  const cudaError_t e = cudaMalloc(&v, count * sizeof(T));
+  if (e != cudaSuccess) return cuda_error(d->ctx, e, "cudaMalloc(dit buffer)");
+  d->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return AEX_OK;
+}
+
+std::string blk(const char* kind, int i, const char* leaf) {
+  return std::string(kind) + "." + std::to_string(i) + "." + leaf;
+}
+
+// Concatenate three [n, k] tile-layout weights along n into one (their n must
+// be multiples of the 256-row tile, so the chunks simply follow each other).
+int fuse3(aex_dit* d, const std::string& a, const std::string& b, const std::string& c, const std::string& out,
+          cudaStream_t s) {
+  auto ia = d->lin.find(a), ib = d->lin.find(b), ic = d->lin.find(c);
+  if (ia == d->lin.end() || ib == d->lin.end() || ic == d->lin.end())
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "missing linear among %s / %s / %s", a.c_str(), b.c_str(),
+                     c.c_str());
+  aex_qweight* w[3] = {ia->second, ib->second, ic->second};
+  for (auto* x : w)
+    if (x->k != w[0]->k || x->n % 256)
+      return set_error(d->ctx, AEX_ERR_UNSUPPORTED, "cannot fuse %s: shapes differ or n %% 256 != 0", out.c_str());
+  auto* f = new aex_qweight();
+  f->device = d->ctx->device;
+  f->n = w[0]->n + w[1]->n + w[2]->n;
+  f->k = w[0]->k;
+  f->n_tiles = w[0]->n_tiles + w[1]->n_tiles + w[2]->n_tiles;
+  f->k_blocks = w[0]->k_blocks;
+  f->bytes = w[0]->bytes + w[1]->bytes + w[2]->bytes;
+  cudaError_t e = cudaMalloc(&f->tiles, f->bytes);
+  if (e != cudaSuccess) {
+    delete f;
+    return cuda_error(d->ctx, e, "cudaMalloc(fused qkv)");
+  }
+  size_t off = 0;
+  for (auto* x : w) {
+    e = cudaMemcpyAsync(f->tiles + off, x->tiles, x->bytes, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_error(d->ctx, e, "cudaMemcpyAsync(fused qkv)");
+    off += x->bytes;
+  }
+  d->lin[out] = f;
+  return AEX_OK;
+}
+
+const aex_qweight* need_lin(aex_dit* d, const std::string& name, int n, int k) {
+  auto it = d->lin.find(name);
+  if (it == d->lin.end()) {
+    set_error(d->ctx, AEX_ERR_INVALID_ARG, "linear '%s' not loaded", name.c_str());
+    return nullptr;
+  }
+  if (it->second->n != n || it->second->k != k) {
+    set_error(d->ctx, AEX_ERR_INVALID_ARG, "linear '%s' is [%d, %d], expected [%d, %d]", name.c_str(), it->second->n,
+              it->second->k, n, k);
+    return nullptr;
+  }
+  return it->second;
+}
+
+const float* need_norm(aex_dit* d, const std::string& name) {
+  auto it = d->norms.find(name);
+  if (it == d->norms.end()) {
+    set_error(d->ctx, AEX_ERR_INVALID_ARG, "norm '%s' not loaded", name.c_str());
+    return nullptr;
+  }
+  return it->second;
+}
+
+#define AEX_TRY(expr)           \
+  do {                          \
+    if (int _r = (expr)) return _r; \
+  } while (0)
+
+#define AEX_NEED(var, expr)              \
+  auto var = (expr);                     \
+  if (!var) return AEX_ERR_INVALID_ARG;
+
+// Joint attention on prepared operands: q/k in PREP (head-major), v and out
+// strided views of the engine's buffers.
+int attend(aex_dit* d, const uint16_t* v, int64_t v_ld, uint16_t* out, int64_t out_ld, cudaStream_t s) {
+  const int J = d->J, H = d->H;
+  const int64_t plane = static_cast<int64_t>(H) * J * 128;
+  aex_attention_args a{};
+  a.q = {d->PREP, plane, 128, static_cast<int64_t>(J) * 128};
+  a.k = {d->PREP + plane, plane, 128, static_cast<int64_t>(J) * 128};
+  a.v = {const_cast<uint16_t*>(v), static_cast<int64_t>(J) * v_ld, v_ld, 128};
+  a.out = {out, static_cast<int64_t>(J) * out_ld, out_ld, 128};
+  a.batch = 1;
+  a.seq = J;
+  a.heads = H;
+  a.head_dim = 128;
+  a.scale = 1.0f / std::sqrt(128.0f);
+  return joint_attention_impl(d->ctx, &a, nullptr, 0, s);
+}
+
+int double_block(aex_dit* d, int i, cudaStream_t s) {
+  const int C = d->C, J = d->J, lt = d->cfg.l_txt, li = d->cfg.l_img, mlp = d->mlp;
+  const float eps_ln = d->cfg.ln_eps;
+  float* Xt = d->X;
+  float* Xi = d->X + static_cast<int64_t>(lt) * C;
+  uint16_t* NHt = d->NH;
+  uint16_t* NHi = d->NH + static_cast<int64_t>(lt) * C;
+  const float* mi = d->MOD_IMG;  // set 0 (msa): shift, scale, gate at 0, C, 2C; set 1 (mlp) at 3C...
+  const float* mt = d->MOD_TXT;
+  AEX_NEED(qkv_i, need_lin(d, blk("transformer_blocks", i, "attn.qkv"), 3 * C, C));
+  AEX_NEED(qkv_t, need_lin(d, blk("transformer_blocks", i, "attn.add_qkv"), 3 * C, C));
+  AEX_NEED(out_i, need_lin(d, blk("transformer_blocks", i, "attn.to_out"), C, C));
+  AEX_NEED(out_t, need_lin(d, blk("transformer_blocks", i, "attn.to_add_out"), C, C));
+  AEX_NEED(ffi_i, need_lin(d, blk("transformer_blocks", i, "ff.linear_in"), 2 * mlp, C));
+  AEX_NEED(ffo_i, need_lin(d, blk("transformer_blocks", i, "ff.linear_out"), C, mlp));
+  AEX_NEED(ffi_t, need_lin(d, blk("transformer_blocks", i, "ff_context.linear_in"), 2 * mlp, C));
+  AEX_NEED(ffo_t, need_lin(d, blk("transformer_blocks", i, "ff_context.linear_out"), C, mlp));
+  AEX_NEED(nq, need_norm(d, blk("transformer_blocks", i, "attn.norm_q")));
+  AEX_NEED(nk, need_norm(d, blk("transformer_blocks", i, "attn.norm_k")));
+  AEX_NEED(naq, need_norm(d, blk("transformer_blocks", i, "attn.norm_added_q")));
+  AEX_NEED(nak, need_norm(d, blk("transformer_blocks", i, "attn.norm_added_k")));
+  // attention half
+  AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + C, mt, eps_ln, NHt, C, s));
+  AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + C, mi, eps_ln, NHi, C, s));
+  const int64_t pq = 3 * C;  // PROJ row pitch for Q|K|V
+  AEX_TRY(qmm_run(d->ctx, qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr, s));
+  const int64_t qs[3] = {static_cast<int64_t>(J) * pq, pq, 128};
+  AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, d->H, nq, nk, naq, nak, lt, d->cfg.rms_eps, d->COS,
+                         d->SIN, d->PREP, s));
+  AEX_TRY(attend(d, d->PROJ + 2 * C, pq, d->ATT, C, s));
+  AEX_TRY(qmm_run(d->ctx, out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C, s));
+  AEX_TRY(qmm_run(d->ctx, out_i, d->ATT + static_cast<int64_t>(lt) * C, C, li, Xi, C, 2, mi + 2 * C, s));
+  // MLP half (per stream)
+  AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + 4 * C, mt + 3 * C, eps_ln, NHt, C, s));
+  AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + 4 * C, mi + 3 * C, eps_ln, NHi, C, s));
+  const int64_t pf = 2 * mlp;
+  uint16_t* SWt = d->ATT;                                   // [lt, mlp]
+  uint16_t* SWi = d->ATT + static_cast<int64_t>(lt) * mlp;  // [li, mlp]
+  AEX_TRY(qmm_run(d->ctx, ffi_t, NHt, C, lt, d->PROJ, pf, 0, nullptr, s));
+  AEX_TRY(glue::swiglu(d->ctx, d->PROJ, d->PROJ + mlp, pf, lt, mlp, SWt, mlp, s));
+  AEX_TRY(qmm_run(d->ctx, ffo_t, SWt, mlp, lt, Xt, C, 2, mt + 5 * C, s));
+  uint16_t* Pi = d->PROJ + static_cast<int64_t>(lt) * pf;
+  AEX_TRY(qmm_run(d->ctx, ffi_i, NHi, C, li, Pi, pf, 0, nullptr, s));
+  AEX_TRY(glue::swiglu(d->ctx, Pi, Pi + mlp, pf, li, mlp, SWi, mlp, s));
+  AEX_TRY(qmm_run(d->ctx, ffo_i, SWi, mlp, li, Xi, C, 2, mi + 5 * C, s));
+  return AEX_OK;
+}
+
+int single_block(aex_dit* d, int i, cudaStream_t s) {
+  const int C = d->C, J = d->J, mlp = d->mlp;
+  AEX_NEED(proj, need_lin(d, blk("single_transformer_blocks", i, "attn.to_qkv_mlp_proj"), d->proj, C));
+  AEX_NEED(out, need_lin(d, blk("single_transformer_blocks", i, "attn.to_out"), C, d->cat));
+  AEX_NEED(nq, need_norm(d, blk("single_transformer_blocks", i, "attn.norm_q")));
+  AEX_NEED(nk, need_norm(d, blk("single_transformer_blocks", i, "attn.norm_k")));
+  const float* ms = d->MOD_SINGLE;
+  AEX_TRY(glue::ln_mod(d->ctx, d->X, C, J, C, ms + C, ms, d->cfg.ln_eps, d->NH, C, s));
+  const int64_t pp = d->proj;
+  AEX_TRY(qmm_run(d->ctx, proj, d->NH, C, J, d->PROJ, pp, 0, nullptr, s));
+  const int64_t qs[3] = {static_cast<int64_t>(J) * pp, pp, 128};
+  AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, d->H, nq, nk, nullptr, nullptr, 0,
+                         d->cfg.rms_eps, d->COS, d->SIN, d->PREP, s));
+  // SwiGLU(g, u) into columns [C, C + mlp) of the concat buffer (ParallelSelfAttention.swift:117-123)
+  AEX_TRY(glue::swiglu(d->ctx, d->PROJ + 3 * C, d->PROJ + 3 * C + mlp, pp, J, mlp, d->ATT + C, d->cat, s));
+  AEX_TRY(attend(d, d->PROJ + 2 * C, pp, d->ATT, d->cat, s));
+  AEX_TRY(qmm_run(d->ctx, out, d->ATT, d->cat, J, d->X, C, 2, ms + 2 * C, s));
+  return AEX_OK;
+}
+
+int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s) {
+  if (!d->rope_set || !d->context_set || !d->timestep_set)
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "set rope, context and timestep before forward");
+  const int C = d->C, lt = d->cfg.l_txt, li = d->cfg.l_img, ic = d->cfg.in_channels;
+  AEX_NEED(xemb, need_lin(d, "x_embedder", C, ic));
+  AEX_NEED(pout, need_lin(d, "proj_out", ic, C));
+  // Fuse the per-stream Q|K|V linears of the double blocks once.
+  for (int i = 0; i < d->cfg.n_double; ++i) {
+    if (!d->lin.count(blk("transformer_blocks", i, "attn.qkv")))
+      AEX_TRY(fuse3(d, blk("transformer_blocks", i, "attn.to_q"), blk("transformer_blocks", i, "attn.to_k"),
+                    blk("transformer_blocks", i, "attn.to_v"), blk("transformer_blocks", i, "attn.qkv"), s));
+    if (!d->lin.count(blk("transformer_blocks", i, "attn.add_qkv")))
+      AEX_TRY(fuse3(d, blk("transformer_blocks", i, "attn.add_q_proj"), blk("transformer_blocks", i, "attn.add_k_proj"),
+                    blk("transformer_blocks", i, "attn.add_v_proj"), blk("transformer_blocks", i, "attn.add_qkv"), s));
+  }
+  // Embedders: image rows from x_embedder (f32 out), text rows from the projected context.
+  AEX_TRY(glue::f32_to_bf16(d->ctx, latents, static_cast<int64_t>(li) * ic, d->LAT16, s));
+  AEX_TRY(qmm_run(d->ctx, xemb, d->LAT16, ic, li, d->X + static_cast<int64_t>(lt) * C, C, 1, nullptr, s));
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->X, d->E0, static_cast<size_t>(lt) * C * 4, cudaMemcpyDeviceToDevice, s));
+  for (int i = 0; i < d->cfg.n_double; ++i) AEX_TRY(double_block(d, i, s));
+  for (int i = 0; i < d->cfg.n_single; ++i) AEX_TRY(single_block(d, i, s));
+  // Head: norm_out (scale | shift) on image rows, proj_out -> f32 velocity.
+  uint16_t* NHi = d->NH + static_cast<int64_t>(lt) * C;
+  AEX_TRY(glue::ln_mod(d->ctx, d->X + static_cast<int64_t>(lt) * C, C, li, C, d->MOD_OUT, d->MOD_OUT + C,
+                       d->cfg.ln_eps, NHi, C, s));
+  AEX_TRY(qmm_run(d->ctx, pout, NHi, C, li, velocity, ic, 1, nullptr, s));
+  return AEX_OK;
+}
+
+// Flux2Scheduler (Sources/ImarelloCore/Flux2Scheduler.swift:20-109): linear mu
+// from the image sequence length, exponential time shift of linspace(1, 1/N, N),
+// terminal 0; timesteps = sigmas * 1000.
+void schedule(int steps, int l_img, std::vector<float>& sigmas, std::vector<float>& timesteps) {
+  const float m = (1.15f - 0.5f) / static_cast<float>(4096 - 256);
+  const float mu = m * static_cast<float>(l_img) + (0.5f - m * 256.0f);
+  sigmas.assign(steps + 1, 0.f);
+  timesteps.assign(steps, 0.f);
+  for (int i = 0; i < steps; ++i) {
+    const float t = steps == 1 ? 1.0f
+                               : 1.0f + (1.0f / static_cast<float>(steps) - 1.0f) * static_cast<float>(i) /
+                                            static_cast<float>(steps - 1);
+    const float e = std::exp(mu);
+    sigmas[i] = e / (e + (1.0f / t - 1.0f));
+    timesteps[i] = sigmas[i] * 1000.0f;
+  }
+}
+
+}  // namespace
+}  // namespace aex
+
+extern "C" {
+
+int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
+  using namespace aex;
+  if (!ctx || !cfg || !out) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  const aex_dit_config& c = *cfg;
+  if (c.hidden <= 0 || c.heads <= 0 || c.hidden != c.heads * 128)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "hidden must be heads * 128 (head_dim 128)");
+  if (c.n_double < 0 || c.n_single < 0 || c.mlp_hidden <= 0 || c.mlp_hidden % 64 || c.hidden % 256 ||
+      c.in_channels % 64 || c.text_dim % 64 || c.timestep_dim % 64 || c.l_txt <= 0 || c.l_img <= 0)
+    return set_error(ctx, AEX_ERR_INVALID_ARG,
+                     "dims must be positive; hidden a multiple of 256; mlp_hidden, in_channels, text_dim, "
+                     "timestep_dim multiples of 64");
+  if (int r = bind_device(ctx)) return r;
+  auto* d = new aex_dit();
+  d->ctx = ctx;
+  d->cfg = c;
+  d->C = c.hidden;
+  d->H = c.heads;
+  d->J = c.l_txt + c.l_img;
+  d->mlp = c.mlp_hidden;
+  d->proj = 3 * c.hidden + 2 * c.mlp_hidden;
+  d->cat = c.hidden + c.mlp_hidden;
+  const size_t J = d->J, C = d->C;
+  const size_t proj_w = std::max<size_t>(d->proj, 2 * static_cast<size_t>(d->mlp));
+  int r = AEX_OK;
+  if (!r) r = dalloc(d, &d->X, J * C);
+  if (!r) r = dalloc(d, &d->E0, static_cast<size_t>(c.l_txt) * C);
+  if (!r) r = dalloc(d, &d->NH, J * C);
+  if (!r) r = dalloc(d, &d->PROJ, J * proj_w);
+  if (!r) r = dalloc(d, &d->ATT, J * static_cast<size_t>(d->cat));
+  if (!r) r = dalloc(d, &d->PREP, 2 * J * C);
+  if (!r) r = dalloc(d, &d->COS, J * 64);
+  if (!r) r = dalloc(d, &d->SIN, J * 64);
+  if (!r) r = dalloc(d, &d->LAT16, static_cast<size_t>(c.l_img) * c.in_channels);
+  if (!r) r = dalloc(d, &d->PRED, static_cast<size_t>(c.l_img) * c.in_channels);
+  if (!r) r = dalloc(d, &d->LATB, static_cast<size_t>(c.l_img) * c.in_channels);
+  if (!r) r = dalloc(d, &d->TSIN, static_cast<size_t>(c.timestep_dim));
+  if (!r) r = dalloc(d, &d->TSIN16, static_cast<size_t>(c.timestep_dim));
+  if (!r) r = dalloc(d, &d->T1, C);
+  if (!r) r = dalloc(d, &d->T16, C);
+  if (!r) r = dalloc(d, &d->TEMB, C);
+  if (!r) r = dalloc(d, &d->MOD_IMG, 6 * C);
+  if (!r) r = dalloc(d, &d->MOD_TXT, 6 * C);
+  if (!r) r = dalloc(d, &d->MOD_SINGLE, 3 * C);
+  if (!r) r = dalloc(d, &d->MOD_OUT, 2 * C);
+  if (r) {
+    aex_dit_destroy(d);
+    return r;
+  }
+  *out = d;
+  return AEX_OK;
+}
+
+void aex_dit_destroy(aex_dit* d) {
+  if (!d) return;
+  cudaSetDevice(d->ctx->device);
+  cudaDeviceSynchronize();
+  for (auto& kv : d->lin) aex_qweight_destroy(kv.second);
+  for (auto& kv : d->norms) cudaFree(kv.second);
+  for (void* p : d->allocs) cudaFree(p);
+  delete d;
+}
+
+int aex_dit_load_linear(aex_dit* d, const char* name, const uint32_t* packed, const uint16_t* scales,
+                        const uint16_t* biases, int n, int k, aex_stream stream) {
+  using namespace aex;
+  if (!d || !name) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  aex_qweight* w = nullptr;
+  if (int r = aex_qweight_create(d->ctx, packed, scales, biases, n, k, 64, 4, &w, stream)) return r;
+  auto it = d->lin.find(name);
+  if (it != d->lin.end()) aex_qweight_destroy(it->second);
+  d->lin[name] = w;
+  // A re-loaded part invalidates a fused Q|K|V built from it.
+  const std::string s(name);
+  for (const char* part : {"attn.to_q", "attn.to_k", "attn.to_v", "attn.add_q_proj", "attn.add_k_proj",
+                           "attn.add_v_proj"}) {
+    const std::string p(part);
+    if (s.size() > p.size() && s.compare(s.size() - p.size(), p.size(), p) == 0) {
+      const std::string prefix = s.substr(0, s.size() - p.size());
+      for (const char* fused : {"attn.qkv", "attn.add_qkv"}) {
+        auto f = d->lin.find(prefix + fused);
+        if (f != d->lin.end()) {
+          aex_qweight_destroy(f->second);
+          d->lin.erase(f);
+        }
+      }
+    }
+  }
+  return AEX_OK;
+}
+
+int aex_dit_load_norm(aex_dit* d, const char* name, const float* weight, aex_stream stream) {
+  using namespace aex;
+  if (!d || !name || !weight) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if (int r = bind_device(d->ctx)) return r;
+  float* w = nullptr;
+  auto it = d->norms.find(name);
+  if (it != d->norms.end()) {
+    w = it->second;
+  } else {
+    AEX_CUDA_TRY(d->ctx, cudaMalloc(&w, 128 * sizeof(float)));
+    d->norms[name] = w;
+  }
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(w, weight, 128 * sizeof(float), cudaMemcpyDeviceToDevice,
+                                       static_cast<cudaStream_t>(stream)));
+  return AEX_OK;
+}
+
+int aex_dit_set_rope(aex_dit* d, const float* cos_t, const float* sin_t, aex_stream stream) {
+  using namespace aex;
+  if (!d || !cos_t || !sin_t) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if (int r = bind_device(d->ctx)) return r;
+  auto s = static_cast<cudaStream_t>(stream);
+  const size_t bytes = static_cast<size_t>(d->J) * 64 * sizeof(float);
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->COS, cos_t, bytes, cudaMemcpyDeviceToDevice, s));
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->SIN, sin_t, bytes, cudaMemcpyDeviceToDevice, s));
+  d->rope_set = true;
+  return AEX_OK;
+}
+
+int aex_dit_project_context(aex_dit* d, const void* embeds, aex_stream stream) {
+  using namespace aex;
+  if (!d || !embeds) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if (int r = bind_device(d->ctx)) return r;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int C = d->C, lt = d->cfg.l_txt;
+  AEX_NEED(ctxemb, need_lin(d, "context_embedder", C, d->cfg.text_dim));
+  // bf16 output (the reference's bf16 qmm), widened to the f32 text residual.
+  AEX_TRY(qmm_run(d->ctx, ctxemb, embeds, d->cfg.text_dim, lt, d->NH, C, 0, nullptr, s));
+  AEX_TRY(glue::bf16_to_f32_rows(d->ctx, d->NH, C, lt, C, d->E0, C, s));
+  d->context_set = true;
+  return AEX_OK;
+}
+
+int aex_dit_set_timestep(aex_dit* d, float timestep, aex_stream stream) {
+  using namespace aex;
+  if (!d) return set_error(nullptr, AEX_ERR_INVALID_ARG, "NULL dit");
+  if (int r = bind_device(d->ctx)) return r;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int C = d->C, td = d->cfg.timestep_dim;
+  AEX_NEED(l1, need_lin(d, "time_guidance_embed.linear_1", C, td));
+  AEX_NEED(l2, need_lin(d, "time_guidance_embed.linear_2", C, C));
+  AEX_NEED(mimg, need_lin(d, "double_stream_modulation_img.linear", 6 * C, C));
+  AEX_NEED(mtxt, need_lin(d, "double_stream_modulation_txt.linear", 6 * C, C));
+  AEX_NEED(msin, need_lin(d, "single_stream_modulation.linear", 3 * C, C));
+  AEX_NEED(mout, need_lin(d, "norm_out.linear", 2 * C, C));
+  AEX_TRY(glue::timestep_embedding(d->ctx, timestep, td, d->TSIN, s));
+  AEX_TRY(glue::f32_to_bf16(d->ctx, d->TSIN, td, d->TSIN16, s));
+  AEX_TRY(qmm_run(d->ctx, l1, d->TSIN16, td, 1, d->T1, C, 1, nullptr, s));
+  AEX_TRY(glue::silu_to_bf16(d->ctx, d->T1, C, d->T16, s));
+  AEX_TRY(qmm_run(d->ctx, l2, d->T16, C, 1, d->TEMB, C, 1, nullptr, s));
+  AEX_TRY(glue::silu_to_bf16(d->ctx, d->TEMB, C, d->T16, s));
+  AEX_TRY(qmm_run(d->ctx, mimg, d->T16, C, 1, d->MOD_IMG, 6 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, mtxt, d->T16, C, 1, d->MOD_TXT, 6 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, msin, d->T16, C, 1, d->MOD_SINGLE, 3 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, mout, d->T16, C, 1, d->MOD_OUT, 2 * C, 1, nullptr, s));
+  d->timestep_set = true;
+  return AEX_OK;
+}
+
+int aex_dit_forward(aex_dit* d, const float* latents, float* velocity, aex_stream stream) {
+  using namespace aex;
+  if (!d || !latents || !velocity) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if (int r = bind_device(d->ctx)) return r;
+  return forward(d, latents, velocity, static_cast<cudaStream_t>(stream));
+}
+
+int aex_dit_denoise_step(aex_dit* d, const float* lat_in, float* lat_out, float dt, aex_stream stream) {
+  using namespace aex;
+  if (!d || !lat_in || !lat_out) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if (int r = bind_device(d->ctx)) return r;
+  auto s = static_cast<cudaStream_t>(stream);
+  AEX_TRY(forward(d, lat_in, d->PRED, s));
+  return glue::euler(d->ctx, lat_in, d->PRED, dt, static_cast<int64_t>(d->cfg.l_img) * d->cfg.in_channels, lat_out,
+                     s);
+}
+
+int aex_dit_denoise(aex_dit* d, float* latents, int steps, aex_stream stream) {
+  using namespace aex;
+  if (!d || !latents || steps < 1) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "bad argument");
+  if (int r = bind_device(d->ctx)) return r;
+  auto s = static_cast<cudaStream_t>(stream);
+  std::vector<float> sig, ts;
+  schedule(steps, d->cfg.l_img, sig, ts);
+  float* cur = latents;
+  float* alt = d->LATB;
+  for (int i = 0; i < steps; ++i) {
+    AEX_TRY(aex_dit_set_timestep(d, ts[i], s));
+    AEX_TRY(aex_dit_denoise_step(d, cur, alt, sig[i + 1] - sig[i], s));
+    std::swap(cur, alt);
+  }
+  if (cur != latents)
+    AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(latents, cur,
+                                         static_cast<size_t>(d->cfg.l_img) * d->cfg.in_channels * sizeof(float),
+                                         cudaMemcpyDeviceToDevice, s));
+  return AEX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,207 @@
+// dit_glue.cu — the elementwise / row-reduction kernels between the DiT's
+// linears and attention calls (all HBM-bound). Restates the arithmetic of the
+// direct engine's glue kernels (Sources/ImarelloDirect/DirectDiTKernels.swift)
+// for a bf16 activation path (the reference's f16 /16 x16 scaling sandwich is
+// not needed with bf16's range):
+//   ln_mod      LayerNorm (no affine, eps) + AdaLN modulate (1+scale)*n + shift -> bf16
+//               (dd_ln_mod_prescale :15-57; Flux2TransformerBlock norm1/modApply,
+//               Sources/ImarelloDiT/TransformerBlock.swift:42-44, ModulationOps.swift)
+//   swiglu      silu(g) * u -> bf16 (dd_swiglu_pitched :138-159; FeedForward.swift:11-24)
+//   gate_add    x += gate * v, x f32 (dd_gate_add :208-221) — used where the
+//               producing GEMM did not already fuse it
+//   euler       lat_out = lat_in + dt * v (Flux2Scheduler.step, Flux2Scheduler.swift:101-109)
+//   timestep    cos/sin sinusoid, flip_sin_to_cos (DirectConditioner.sinusoid,
+//               Sources/ImarelloDirect/DirectConditioner.swift:160-170)
+//   silu, f32 -> bf16, bf16 -> f32 row copies.
+#include "dit_internal.h"
+#include "sm100.cuh"
+
+namespace aex {
+namespace glue {
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (w == 0) {
+    t = l < (blockDim.x >> 5) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (l == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// One CTA per row; C a multiple of 4. Two-pass (mean, then centered variance)
+// in f32 from registers/L1.
+__global__ void __launch_bounds__(kRowThreads) ln_mod_kernel(const float* __restrict__ x, int64_t ldx, int C,
+                                                             const float* __restrict__ scale,
+                                                             const float* __restrict__ shift, float eps,
+                                                             __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  __shared__ float red[32];
+  const float* xr = x + static_cast<int64_t>(blockIdx.x) * ldx;
+  float s = 0.f;
+  for (int i = threadIdx.x * 4; i < C; i += kRowThreads * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    s += (v.x + v.y) + (v.z + v.w);
+  }
+  const float mean = block_sum(s, red) / C;
+  float q = 0.f;
+  for (int i = threadIdx.x * 4; i < C; i += kRowThreads * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  const float inv = rsqrtf(block_sum(q, red) / C + eps);
+  __nv_bfloat16* yr = y + static_cast<int64_t>(blockIdx.x) * ldy;
+  for (int i = threadIdx.x * 4; i < C; i += kRowThreads * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + i));
+    const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + i));
+    const float o0 = fmaf(1.f + sc.x, (v.x - mean) * inv, sh.x);
+    const float o1 = fmaf(1.f + sc.y, (v.y - mean) * inv, sh.y);
+    const float o2 = fmaf(1.f + sc.z, (v.z - mean) * inv, sh.z);
+    const float o3 = fmaf(1.f + sc.w, (v.w - mean) * inv, sh.w);
+    *reinterpret_cast<uint2*>(yr + i) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+  }
+}
+
+// silu(g) * u over [rows, width] with pitched inputs; 8 columns per thread.
+__global__ void swiglu_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, int64_t ld_in,
+                              int rows, int width, uint16_t* __restrict__ out, int64_t ld_out) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int per_row = width / 8;
+  if (idx >= static_cast<int64_t>(rows) * per_row) return;
+  const int64_t r = idx / per_row;
+  const int c = static_cast<int>(idx % per_row) * 8;
+  const uint4 gv = *reinterpret_cast<const uint4*>(g + r * ld_in + c);
+  const uint4 uv = *reinterpret_cast<const uint4*>(u + r * ld_in + c);
+  const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float g0 = bf16lo_to_f32(ga[i]), g1 = bf16hi_to_f32(ga[i]);
+    const float u0 = bf16lo_to_f32(ua[i]), u1 = bf16hi_to_f32(ua[i]);
+    o[i] = pack_bf16x2(g0 / (1.f + __expf(-g0)) * u0, g1 / (1.f + __expf(-g1)) * u1);
+  }
+  *reinterpret_cast<uint4*>(out + r * ld_out + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void gate_add_kernel(float* __restrict__ x, int64_t ldx, int rows, int C, const float* __restrict__ gate,
+                                const uint16_t* __restrict__ v, int64_t ldv, float scale) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * C) return;
+  const int64_t r = idx / C;
+  const int c = static_cast<int>(idx % C);
+  float* xp = x + r * ldx + c;
+  *xp = fmaf(gate ? gate[c] : 1.f, __uint_as_float(static_cast<uint32_t>(v[r * ldv + c]) << 16) * scale, *xp);
+}
+
+__global__ void euler_kernel(const float* __restrict__ lat_in, const float* __restrict__ v, float dt, int64_t n,
+                             float* __restrict__ lat_out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) lat_out[i] = fmaf(dt, v[i], lat_in[i]);
+}
+
+__global__ void timestep_kernel(float t, int dim, float* __restrict__ out) {
+  const int half = dim / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float freq = expf(-logf(10000.0f) * static_cast<float>(i) / static_cast<float>(half));
+    const float arg = t * freq;
+    out[i] = cosf(arg);
+    out[half + i] = sinf(arg);
+  }
+  if (dim % 2 && threadIdx.x == 0) out[dim - 1] = 0.f;
+}
+
+__global__ void silu_to_bf16_kernel(const float* __restrict__ x, int n, uint16_t* __restrict__ y) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float v = x[i];
+    y[i] = static_cast<uint16_t>(pack_bf16x2(v / (1.f + expf(-v)), 0.f) & 0xFFFFu);
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, int64_t n, uint16_t* __restrict__ y) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = static_cast<uint16_t>(pack_bf16x2(x[i], 0.f) & 0xFFFFu);
+}
+
+__global__ void bf16_to_f32_rows_kernel(const uint16_t* __restrict__ x, int64_t ldx, int rows, int cols,
+                                        float* __restrict__ y, int64_t ldy) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(rows) * cols) return;
+  const int64_t r = idx / cols;
+  const int c = static_cast<int>(idx % cols);
+  y[r * ldy + c] = __uint_as_float(static_cast<uint32_t>(x[r * ldx + c]) << 16);
+}
+
+unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
+
+}  // namespace
+
+int ln_mod(aex_ctx* ctx, const float* x, int64_t ldx, int rows, int C, const float* scale, const float* shift,
+           float eps, void* y, int64_t ldy, cudaStream_t s) {
+  if (rows <= 0) return AEX_OK;
+  if (C % 4 || ldx % 4 || ldy % 4) return set_error(ctx, AEX_ERR_INVALID_ARG, "ln_mod: C and pitches must be multiples of 4");
+  ln_mod_kernel<<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, static_cast<__nv_bfloat16*>(y), ldy);
+  return check_launch(ctx, "ln_mod_kernel");
+}
+
+int swiglu(aex_ctx* ctx, const void* g, const void* u, int64_t ld_in, int rows, int width, void* out, int64_t ld_out,
+           cudaStream_t s) {
+  if (rows <= 0) return AEX_OK;
+  if (width % 8 || ld_in % 8 || ld_out % 8) return set_error(ctx, AEX_ERR_INVALID_ARG, "swiglu: widths must be multiples of 8");
+  const int64_t n = static_cast<int64_t>(rows) * (width / 8);
+  swiglu_kernel<<<blocks_for(n, 256), 256, 0, s>>>(static_cast<const uint16_t*>(g), static_cast<const uint16_t*>(u),
+                                                    ld_in, rows, width, static_cast<uint16_t*>(out), ld_out);
+  return check_launch(ctx, "swiglu_kernel");
+}
+
+int gate_add(aex_ctx* ctx, float* x, int64_t ldx, int rows, int C, const float* gate, const void* v, int64_t ldv,
+             float scale, cudaStream_t s) {
+  if (rows <= 0) return AEX_OK;
+  const int64_t n = static_cast<int64_t>(rows) * C;
+  gate_add_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, ldx, rows, C, gate, static_cast<const uint16_t*>(v), ldv,
+                                                      scale);
+  return check_launch(ctx, "gate_add_kernel");
+}
+
+int euler(aex_ctx* ctx, const float* lat_in, const float* v, float dt, int64_t n, float* lat_out, cudaStream_t s) {
+  euler_kernel<<<blocks_for(n, 256), 256, 0, s>>>(lat_in, v, dt, n, lat_out);
+  return check_launch(ctx, "euler_kernel");
+}
+
+int timestep_embedding(aex_ctx* ctx, float t, int dim, float* out, cudaStream_t s) {
+  timestep_kernel<<<1, 128, 0, s>>>(t, dim, out);
+  return check_launch(ctx, "timestep_kernel");
+}
+
+int silu_to_bf16(aex_ctx* ctx, const float* x, int n, void* y, cudaStream_t s) {
+  silu_to_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, n, static_cast<uint16_t*>(y));
+  return check_launch(ctx, "silu_to_bf16_kernel");
+}
+
+int f32_to_bf16(aex_ctx* ctx, const float* x, int64_t n, void* y, cudaStream_t s) {
+  f32_to_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, n, static_cast<uint16_t*>(y));
+  return check_launch(ctx, "f32_to_bf16_kernel");
+}
+
+int bf16_to_f32_rows(aex_ctx* ctx, const void* x, int64_t ldx, int rows, int cols, float* y, int64_t ldy,
+                     cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  bf16_to_f32_rows_kernel<<<blocks_for(n, 256), 256, 0, s>>>(static_cast<const uint16_t*>(x), ldx, rows, cols, y,
+                                                              ldy);
+  return check_launch(ctx, "bf16_to_f32_rows_kernel");
+}
+
+}  // namespace glue
+}  // namespace aex

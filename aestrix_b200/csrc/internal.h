@@ -57,4 +57,18 @@ int make_tmap(aex_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dtype, const v
 // Check the last kernel launch.
 int check_launch(aex_ctx* ctx, const char* what);
 
+// ---- internal entry points shared by the DiT engine (dit_engine.cpp)
+// qmm with an epilogue mode: 0 bf16 out, 1 f32 out, 2 gated residual
+// (y_f32[row, col] += gate[col] * acc). No argument validation beyond m/gate.
+int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy, int mode,
+            const float* gate, cudaStream_t s);
+// QK-RMSNorm + RoPE pre-pass into head-major scratch [2][B][H][S][128]; tokens
+// s < split use (wq_a, wk_a), the others (wq, wk).
+int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
+                   int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
+                   float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream);
+// Attention (and prep if args ask for it) on validated args.
+int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
+                         cudaStream_t stream);
+
 }  // namespace aex

@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(256) dequant_mlx_kernel(const uint32_t* __rest
 }
 
 // ------------------------------------------------------------------ K2 GEMM
+enum OutMode : int { kOutBf16 = 0, kOutF32 = 1, kOutResidualGate = 2 };
+
 constexpr int kGemmThreads = 640;  // warps 0 producer, 1 UMMA, 2-3 idle, 4-19 dequant + epilogue
 constexpr int kDequantWarp0 = 4;
 constexpr int kDequantThreads = 512;  // one half-row (4 packed words, 32 codes) per thread per K block
@@ -147,7 +149,8 @@ struct GemmParams {
   int m, n, k_blocks;
   void* y;
   int64_t ldy;
-  int y_f32;
+  int mode;           // kOutBf16, kOutF32, kOutResidualGate
+  const float* gate;  // kOutResidualGate: y_f32[row, col] += gate[col] * acc
   int vec;  // y base and row pitch are 16-byte aligned: full 32-column runs use 16-byte stores
 };
 
@@ -285,7 +288,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_wait_ld();
           const int col = n0 + c0;
           if (row < p.m && col < p.n) {
-            if (p.y_f32) {
+            if (p.mode == kOutResidualGate) {
+              // Gated residual (dd_gate_add, DirectDiTKernels.swift:208-221): y += gate * acc, f32.
+              float* yr = static_cast<float*>(p.y) + static_cast<int64_t>(row) * p.ldy + col;
+              if (p.vec && col + 32 <= p.n) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                  const float4 g = __ldg(reinterpret_cast<const float4*>(p.gate + col + i));
+                  float4 v = *reinterpret_cast<float4*>(yr + i);
+                  v.x = fmaf(g.x, __uint_as_float(r[i]), v.x);
+                  v.y = fmaf(g.y, __uint_as_float(r[i + 1]), v.y);
+                  v.z = fmaf(g.z, __uint_as_float(r[i + 2]), v.z);
+                  v.w = fmaf(g.w, __uint_as_float(r[i + 3]), v.w);
+                  *reinterpret_cast<float4*>(yr + i) = v;
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (col + i < p.n) yr[i] = fmaf(p.gate[col + i], __uint_as_float(r[i]), yr[i]);
+              }
+            } else if (p.mode == kOutF32) {
               float* yr = static_cast<float*>(p.y) + static_cast<int64_t>(row) * p.ldy + col;
               if (p.vec && col + 32 <= p.n) {
 #pragma unroll
@@ -337,7 +359,8 @@ struct GemvParams {
   int m, n, k_blocks, kb_per_split;
   void* y;
   int64_t ldy;
-  int y_f32;
+  int mode;
+  const float* gate;
 };
 
 template <int R>
@@ -434,7 +457,9 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
       float v = 0.f;
       for (int c = 0; c < static_cast<int>(gridDim.y); ++c)
         v += ld_shared_cluster_f32(mapa_shared(my_part + (mr * kGemvRows + t) * 4, c));
-      if (p.y_f32)
+      if (p.mode == kOutResidualGate)
+        static_cast<float*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] += p.gate[row] * v;
+      else if (p.mode == kOutF32)
         static_cast<float*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] = v;
       else
         static_cast<uint16_t*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] =
@@ -463,7 +488,7 @@ int validate_q(aex_ctx* ctx, const void* packed, const void* scales, const void*
 
 template <int MT>
 int launch_gemm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
-                int y_f32, cudaStream_t s) {
+                int mode, const float* gate, cudaStream_t s) {
   using L = qmm::GemmLayout<MT>;
   CUtensorMap tx;
   uint64_t dims[2] = {static_cast<uint64_t>(w->k), static_cast<uint64_t>(m)};
@@ -472,9 +497,12 @@ int launch_gemm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
   if (int r = make_tmap(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, 2, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B))
     return r;
-  const int esz = y_f32 ? 4 : 2;
-  const int vec = ((reinterpret_cast<uintptr_t>(y) & 15) == 0 && (ldy * esz) % 16 == 0) ? 1 : 0;
-  qmm::GemmParams p{w->tiles, m, w->n, w->k_blocks, y, ldy, y_f32, vec};
+  const int esz = mode == qmm::kOutBf16 ? 2 : 4;
+  const int vec = ((reinterpret_cast<uintptr_t>(y) & 15) == 0 && (ldy * esz) % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(gate) & 15) == 0)
+                      ? 1
+                      : 0;
+  qmm::GemmParams p{w->tiles, m, w->n, w->k_blocks, y, ldy, mode, gate, vec};
   auto kern = qmm::gemm_kernel<MT>;
   AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem));
   dim3 grid(w->n_tiles, (m + 128 * MT - 1) / (128 * MT));
@@ -484,7 +512,7 @@ int launch_gemm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
 
 template <int R>
 int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
-                int y_f32, cudaStream_t s) {
+                int mode, const float* gate, cudaStream_t s) {
   const int n_ctas = (w->n + qmm::kGemvRows - 1) / qmm::kGemvRows;
   // Enough CTAs to cover every SM several times, and at most kGemvMaxKbps K blocks per CTA.
   int split = std::max(1, std::min(qmm::kGemvMaxSplit, (4 * ctx->sm_count + n_ctas - 1) / n_ctas));
@@ -502,7 +530,7 @@ int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
   split = (w->k_blocks + kbps - 1) / kbps;
   AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(qmm::gemv_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kMaxSmem)));
-  qmm::GemvParams p{static_cast<const uint16_t*>(x), ldx, w->tiles, m, w->n, w->k_blocks, kbps, y, ldy, y_f32};
+  qmm::GemvParams p{static_cast<const uint16_t*>(x), ldx, w->tiles, m, w->n, w->k_blocks, kbps, y, ldy, mode, gate};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(n_ctas, split, 1);
   cfg.blockDim = dim3(qmm::kGemvRows, 1, 1);
@@ -520,6 +548,22 @@ int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
 }
 
 }  // namespace
+
+int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy, int mode,
+            const float* gate, cudaStream_t s) {
+  if (m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
+  if (mode == qmm::kOutResidualGate && !gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
+  if (m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps) {
+    if (m <= 1) return launch_gemv<1>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+    if (m <= 2) return launch_gemv<2>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+    if (m <= 4) return launch_gemv<4>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+    if (m <= 8) return launch_gemv<8>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+    return launch_gemv<16>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+  }
+  if (m >= 2048) return launch_gemm<2>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+  return launch_gemm<1>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+}
+
 }  // namespace aex
 
 extern "C" {
@@ -609,17 +653,8 @@ int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int 
     return set_error(ctx, AEX_ERR_INVALID_ARG, "y must be aligned to its element size with ldy >= n");
   if (ctx->device != w->device) return set_error(ctx, AEX_ERR_INVALID_ARG, "weight lives on another device");
   if (int r = bind_device(ctx)) return r;
-  auto s = static_cast<cudaStream_t>(stream);
-  const int f32 = y_dtype == AEX_DTYPE_F32;
-  if (m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps) {
-    if (m <= 1) return launch_gemv<1>(ctx, w, x, ldx, m, y, ldy, f32, s);
-    if (m <= 2) return launch_gemv<2>(ctx, w, x, ldx, m, y, ldy, f32, s);
-    if (m <= 4) return launch_gemv<4>(ctx, w, x, ldx, m, y, ldy, f32, s);
-    if (m <= 8) return launch_gemv<8>(ctx, w, x, ldx, m, y, ldy, f32, s);
-    return launch_gemv<16>(ctx, w, x, ldx, m, y, ldy, f32, s);
-  }
-  if (m >= 2048) return launch_gemm<2>(ctx, w, x, ldx, m, y, ldy, f32, s);
-  return launch_gemm<1>(ctx, w, x, ldx, m, y, ldy, f32, s);
+  return qmm_run(ctx, w, x, ldx, m, y, ldy, y_dtype == AEX_DTYPE_F32 ? qmm::kOutF32 : qmm::kOutBf16, nullptr,
+                 static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -193,6 +193,70 @@ int aex_qweight_dequantize(aex_ctx* ctx, const aex_qweight* w, uint16_t* out, ae
 int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
             int y_dtype, aex_stream stream);
 
+/* ------------------------------------------------------------ DiT engine */
+
+/* The FLUX.2-klein transformer denoise step on one device: the direct
+ * engine's static-plan step (DirectDiTStep, Sources/ImarelloDirect/
+ * DirectDiTStep.swift:11-977) plus its conditioner (DirectConditioner,
+ * Sources/ImarelloDirect/DirectConditioner.swift:14-255) and the packed-latent
+ * denoiser (DirectDiTPackedDenoiser.denoise, DirectDiTAdapter.swift:25-81).
+ * head_dim is 128. Klein 4B: hidden 3072, heads 24, 5 double + 20 single
+ * blocks, mlp_hidden 9216, in_channels 128, text_dim 7680, timestep_dim 256,
+ * l_txt 512, l_img = (W/16)*(H/16), rms_eps 1e-5, ln_eps 1e-6. */
+typedef struct aex_dit aex_dit;
+
+typedef struct aex_dit_config {
+  int hidden;
+  int heads;
+  int n_double;
+  int n_single;
+  int mlp_hidden;
+  int in_channels;
+  int text_dim;
+  int timestep_dim;
+  int l_txt;
+  int l_img;
+  float rms_eps;
+  float ln_eps;
+} aex_dit_config;
+
+/* Allocates the engine's static buffer plan (DirectDiTStep.allocateScratch,
+ * DirectDiTStep.swift:155-274). */
+int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out);
+void aex_dit_destroy(aex_dit* dit);
+
+/* Upload one 4-bit linear from its MLX arrays (device pointers: packed uint32
+ * [n, k/8], bf16 scales/biases [n, k/64]) under its MLX key, e.g.
+ * "transformer_blocks.0.attn.to_q", "single_transformer_blocks.3.attn.to_out",
+ * "x_embedder", "norm_out.linear" (DirectDiTStep.quant/loadBlocks/loadHead,
+ * DirectDiTStep.swift:278-335, 844-884; DirectConditioner.init :30-83). */
+int aex_dit_load_linear(aex_dit* dit, const char* name, const uint32_t* packed, const uint16_t* scales,
+                        const uint16_t* biases, int n, int k, aex_stream stream);
+/* Upload one RMSNorm weight ([128] f32 device), e.g.
+ * "transformer_blocks.0.attn.norm_added_q" (DirectDiTStep.normW :285-293). */
+int aex_dit_load_norm(aex_dit* dit, const char* name, const float* weight, aex_stream stream);
+/* Rotary tables [l_txt + l_img, 64] f32 (device), text rows first
+ * (DirectConditioner.rope; setConditioning cos/sin, DirectDiTStep.swift:337-355). */
+int aex_dit_set_rope(aex_dit* dit, const float* cos_t, const float* sin_t, aex_stream stream);
+/* Context embedding: bf16 [l_txt, text_dim] -> context_embedder (4-bit,
+ * bf16 output) -> f32 text residual (DirectConditioner.projectContext :217-240). */
+int aex_dit_project_context(aex_dit* dit, const void* embeds, aex_stream stream);
+/* Per-step conditioning on the device for one timestep (sigma * 1000):
+ * sinusoid -> time MLP -> SiLU -> modulation heads and norm_out
+ * (DirectConditioner.stepConditioning :172-213, setStepConditioning
+ * DirectDiTStep.swift:887-904). */
+int aex_dit_set_timestep(aex_dit* dit, float timestep, aex_stream stream);
+/* One transformer pass: latents f32 [l_img, in_channels] -> predicted velocity
+ * f32 [l_img, in_channels] (x_embedder, 25 blocks, norm_out, proj_out;
+ * DirectDiTStep.encodeDenoiseStep :908-950 without the Euler update). */
+int aex_dit_forward(aex_dit* dit, const float* latents, float* velocity, aex_stream stream);
+/* forward + Euler update lat_out = lat_in + dt * v (encodeDenoiseStep :908-971). */
+int aex_dit_denoise_step(aex_dit* dit, const float* lat_in, float* lat_out, float dt, aex_stream stream);
+/* The whole denoise: Flux2Scheduler(steps, l_img) (Flux2Scheduler.swift:20-109),
+ * per step set_timestep + denoise_step; `latents` holds the noise on entry and
+ * the result on return (DirectDiTPackedDenoiser.denoise :25-81). */
+int aex_dit_denoise(aex_dit* dit, float* latents, int steps, aex_stream stream);
+
 /* -------------------------------------------------------------- self test */
 
 /* Tensor-core path self test (no reference counterpart; a device bring-up

@@ -191,6 +191,15 @@ def schedule(steps, image_seq_len):
     return sig, ts
 
 
+def ln_mod_rows(x, scale, shift, eps):
+    """LayerNorm (no affine) + (1 + scale) * n + shift over rows [r, d] (aexo_ln_mod)."""
+    x = _c(x, np.float32)
+    rows, d = x.shape
+    y = np.empty_like(x)
+    lib().aexo_ln_mod(x, rows, d, _c(scale, np.float32), _c(shift, np.float32), eps, y)
+    return y
+
+
 def timestep_embedding(t, dim=256):
     t = _c(t, np.float32)
     out = np.empty((t.size, dim), np.float32)
