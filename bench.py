@@ -297,6 +297,52 @@ def measure_qmm(ctx, dev, iters=20):
     return out
 
 
+def measure_dit(ctx, dev, world, runs=3):
+    """the full FLUX.2-klein 4-step denoise at 1024^2 on random-init 4-bit weights
+    (hidden 3072, 24 heads, 5 double + 20 single blocks, mlp 9216), context 512 x 7680 bf16 N(0,1),
+    latents 4096 x 128 f32 N(0,1); one image per GPU. Device time of aex_dit_denoise (4 x conditioning +
+    transformer + Euler), context projection excluded (once per generate); max over ranks."""
+    import torch
+
+    from aestrix_b200 import dit
+
+    cfg = dit.DitConfig()
+    lin, norms = dit.random_weights(cfg, seed=11, device=dev)
+    eng = dit.DitEngine(cfg, ctx=ctx, device=dev.index)
+    eng.load(lin, norms)
+    del lin
+    cos, sin = dit.rope_tables(cfg, device=dev)
+    eng.set_rope(cos, sin)
+    g = torch.Generator().manual_seed(99)
+    embeds = torch.randn(cfg.l_txt, cfg.text_dim, generator=g).to(torch.bfloat16).to(dev)
+    noise = torch.randn(cfg.l_img, cfg.in_channels, generator=torch.Generator().manual_seed(42)).to(dev)
+    eng.project_context(embeds)
+    lat = noise.clone()
+    eng.denoise(lat, steps=4)  # warm-up (also builds the fused Q|K|V weights)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    times = []
+    for _ in range(runs):
+        lat.copy_(noise)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        eng.denoise(lat, steps=4, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = _max_over_ranks(world, min(times))
+    fl = dit.dit_flops(cfg)
+    ok = bool(torch.isfinite(lat).all().item())
+    eng.close()
+    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "images_per_s": world * 4000.0 / ms / 4,
+            "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12, "tflop_per_step": fl["total"] / 1e12,
+            "flops_split_per_step": {"linear": fl["linear"] / 1e12, "attention": fl["attention"] / 1e12},
+            "n_gpus": world, "batch": world, "finite": ok,
+            "config": "BASELINE configs[3]: FLUX.2-klein 1024^2, 4 steps, random-init 4-bit weights, 1 image/GPU"}
+
+
 def run_ours(args):
     import torch
 
@@ -393,6 +439,7 @@ def run_ours(args):
     _barrier(world)
 
     qmm_res = measure_qmm(ctx, dev) if not args.no_qmm else None
+    dit_res = measure_dit(ctx, dev, world) if not args.no_dit else None
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = FLOPS_PER_CALL / (kernel_ms * 1e-3) / 1e12
@@ -415,6 +462,8 @@ def run_ours(args):
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
+        if dit_res is not None:
+            line["dit_denoise"] = dit_res
         if qmm_res is not None:
             hbm = _hbm_peak()
             for v in qmm_res.values():
@@ -438,6 +487,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=SEQ, help="query rows in the CPU-baseline sample")
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target duration of the reference arm")
     ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
+    ap.add_argument("--no-dit", action="store_true", help="skip the secondary 4-step DiT denoise measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
