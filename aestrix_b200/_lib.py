@@ -110,6 +110,11 @@ _SIGNATURES = [
     ("aex_dit_forward", C.c_int, [_VP, _VP, _VP, _VP]),
     ("aex_dit_denoise_step", C.c_int, [_VP, _VP, _VP, C.c_float, _VP]),
     ("aex_dit_denoise", C.c_int, [_VP, _VP, C.c_int, _VP]),
+    ("aex_comm_unique_id", C.c_int, [_VP]),
+    ("aex_comm_create", C.c_int, [_VP, C.c_int, C.c_int, _VP, C.c_int, C.POINTER(_VP)]),
+    ("aex_comm_destroy", None, [_VP]),
+    ("aex_comm_abort", C.c_int, [_VP]),
+    ("aex_ring_attention", C.c_int, [_VP, _VP, C.POINTER(aex_attention_args), _VP]),
     ("aex_selftest_umma", C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
 ]
 

@@ -96,9 +96,15 @@ constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
 
 struct Params {
-  int seq;
+  int seq;       // query rows
+  int seq_kv;    // key/value rows (== seq except for ring-attention hops)
   int n_kv;
   float scale_log2;
+  // Optional per-row log-sum-exp of the scaled scores in log2 units,
+  // lse2 = m + log2(l), stored at lse[b * lse_sb + h * lse_sh + row]; lets
+  // partial results over different K/V sets be merged exactly.
+  float* lse;
+  int64_t lse_sb, lse_sh;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -290,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       uint32_t r[128];
-      const int valid = p.seq - j * kBN;
+      const int valid = p.seq_kv - j * kBN;
       float mx0, mx1, mx2, mx3;
       auto mask_chunk = [&](int c0) {
         if (valid < kBN) {
@@ -396,6 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
+      if (p.lse && q0 + t * kBM + row < p.seq)
+        p.lse[b * p.lse_sb + h * p.lse_sh + q0 + t * kBM + row] = m_run + __log2f(l_run);
 #pragma unroll 1
       for (int cc = 0; cc < 128; cc += 32) {
         uint32_t o[32];
@@ -657,22 +665,30 @@ int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratc
     ks[1] = qs[1];
     ks[2] = qs[2];
   }
+  return launch_attention_core(ctx, qsrc, qs, ksrc, ks, a->v.data, &a->v.stride_b, a->out.data, &a->out.stride_b, B,
+                               S, S, H, a->scale, nullptr, 0, 0, stream);
+}
+
+int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
+                          const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
+                          float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream) {
   CUtensorMap tq, tk, tv, to;
-  if (int r = bshd_tmap(ctx, &tq, qsrc, qs[0], qs[1], qs[2], B, S, H)) return r;
-  if (int r = bshd_tmap(ctx, &tk, ksrc, ks[0], ks[1], ks[2], B, S, H)) return r;
-  if (int r = bshd_tmap(ctx, &tv, a->v.data, a->v.stride_b, a->v.stride_s, a->v.stride_h, B, S, H)) return r;
-  if (int r = bshd_tmap(ctx, &to, a->out.data, a->out.stride_b, a->out.stride_s, a->out.stride_h, B, S, H)) return r;
+  if (int r = bshd_tmap(ctx, &tq, q, qs[0], qs[1], qs[2], B, S, H)) return r;
+  if (int r = bshd_tmap(ctx, &tk, k, ks[0], ks[1], ks[2], B, S_kv, H)) return r;
+  if (int r = bshd_tmap(ctx, &tv, v, vs[0], vs[1], vs[2], B, S_kv, H)) return r;
+  if (int r = bshd_tmap(ctx, &to, o, os[0], os[1], os[2], B, S, H)) return r;
   attn::Params prm{};
   prm.seq = S;
-  prm.n_kv = (S + attn::kBN - 1) / attn::kBN;
-  const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(128.0f);
-  prm.scale_log2 = scale * 1.4426950408889634f;
-  static bool attr_set = false;
-  if (!attr_set) {
-    AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           attn::kSmemBytes));
-    attr_set = true;
-  }
+  prm.seq_kv = S_kv;
+  prm.n_kv = (S_kv + attn::kBN - 1) / attn::kBN;
+  const float sc = scale > 0.f ? scale : 1.0f / std::sqrt(128.0f);
+  prm.scale_log2 = sc * 1.4426950408889634f;
+  prm.lse = lse;
+  prm.lse_sb = lse_sb;
+  prm.lse_sh = lse_sh;
+  // Per call (cheap): the attribute is per device, and a process may drive several.
+  AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         attn::kSmemBytes));
   dim3 grid((S + attn::kTiles * attn::kBM - 1) / (attn::kTiles * attn::kBM), H, B);
   attn::attn_fwd_kernel<<<grid, attn::kThreads, attn::kSmemBytes, stream>>>(tq, tk, tv, to, prm, ctx->d_status);
   return check_launch(ctx, "attn_fwd_kernel");

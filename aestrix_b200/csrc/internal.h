@@ -67,6 +67,12 @@ int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int 
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
                    int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
                    float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream);
+// The attention kernel on prepared operands: strided [B, S, H, 128] views
+// (strides in elements: batch, seq, head) for Q/O with S rows and K/V with
+// S_kv rows; optional per-row log2-sum-exp output lse[b*lse_sb + h*lse_sh + row].
+int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
+                          const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
+                          float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream);
 // Attention (and prep if args ask for it) on validated args.
 int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
                          cudaStream_t stream);

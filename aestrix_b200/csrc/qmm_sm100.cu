@@ -560,7 +560,10 @@ int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int 
     if (m <= 8) return launch_gemv<8>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
     return launch_gemv<16>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
   }
-  if (m >= 2048) return launch_gemm<2>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+#ifndef AEX_QMM_MT2_MIN_M
+#define AEX_QMM_MT2_MIN_M 2048
+#endif
+  if (m >= AEX_QMM_MT2_MIN_M) return launch_gemm<2>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
   return launch_gemm<1>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
 }
 

@@ -1,0 +1,280 @@
+// ring_attention.cpp — sequence-parallel joint attention over P GPUs (one
+// process per GPU) for long sequences (2048^2: 512 text + 16384 image tokens).
+//
+// The reference keeps the full sequence on one device (ParallelSelfAttention
+// runs one SDPA over full-length Q/K/V, Sources/ImarelloDiT/ParallelSelfAttention.swift:
+// 134-136); this is the multi-GPU form of the same computation. The joint
+// sequence is split into P equal contiguous shards (rank r holds tokens
+// [r*S_r, (r+1)*S_r), text rows in shard 0). Each rank RMS-normalizes and
+// rotates its own Q and K rows (RoPE uses absolute positions, so rotating
+// before the exchange is exact), then for hop h = 0..P-1 attends its queries to
+// the K/V shard of rank (r - h) mod P while the next shard travels around the
+// ring (ncclSend to r+1 / ncclRecv from r-1 on a dedicated stream, double
+// buffered). Partial outputs are merged by their log-sum-exp
+// (ring_kernels.cu).
+//
+// NCCL is resolved at run time (the copy already loaded in the process, else
+// libnccl.so.2), so the library has no link-time NCCL dependency.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <thread>
+
+#include "internal.h"
+
+namespace aex {
+namespace ring {
+int merge(aex_ctx* ctx, const void* o_h, int64_t oh_ss, int64_t oh_sh, const float* lse_h, const float* lse_in,
+          float* lse_out, float* o_acc, int S, int H, bool first, bool final, void* out, int64_t out_ss, int64_t out_sh,
+          cudaStream_t s);
+}
+
+namespace {
+
+struct NcclApi {
+  decltype(&ncclGetUniqueId) getUniqueId = nullptr;
+  decltype(&ncclCommInitRankConfig) commInitRankConfig = nullptr;
+  decltype(&ncclCommDestroy) commDestroy = nullptr;
+  decltype(&ncclCommAbort) commAbort = nullptr;
+  decltype(&ncclCommGetAsyncError) commGetAsyncError = nullptr;
+  decltype(&ncclSend) send = nullptr;
+  decltype(&ncclRecv) recv = nullptr;
+  decltype(&ncclGroupStart) groupStart = nullptr;
+  decltype(&ncclGroupEnd) groupEnd = nullptr;
+  decltype(&ncclGetErrorString) errorString = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen(nullptr, RTLD_NOW);  // prefer a copy already in the process (e.g. torch's)
+    if (!h || !dlsym(h, "ncclGetUniqueId")) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    auto sym = [&](auto& f, const char* name) { f = reinterpret_cast<std::remove_reference_t<decltype(f)>>(dlsym(h, name)); };
+    sym(api.getUniqueId, "ncclGetUniqueId");
+    sym(api.commInitRankConfig, "ncclCommInitRankConfig");
+    sym(api.commDestroy, "ncclCommDestroy");
+    sym(api.commAbort, "ncclCommAbort");
+    sym(api.commGetAsyncError, "ncclCommGetAsyncError");
+    sym(api.send, "ncclSend");
+    sym(api.recv, "ncclRecv");
+    sym(api.groupStart, "ncclGroupStart");
+    sym(api.groupEnd, "ncclGroupEnd");
+    sym(api.errorString, "ncclGetErrorString");
+    api.ok = api.getUniqueId && api.commInitRankConfig && api.commDestroy && api.commAbort && api.commGetAsyncError &&
+             api.send && api.recv && api.groupStart && api.groupEnd && api.errorString;
+  });
+  return api;
+}
+
+int nccl_error(aex_ctx* ctx, ncclResult_t r, const char* what) {
+  return set_error(ctx, AEX_ERR_NCCL, "%s failed: %s", what, nccl().errorString ? nccl().errorString(r) : "?");
+}
+
+}  // namespace
+}  // namespace aex
+
+struct aex_comm {
+  aex_ctx* ctx = nullptr;
+  ncclComm_t comm = nullptr;
+  int world = 0, rank = 0;
+  cudaStream_t stream = nullptr;  // exchange stream
+  cudaEvent_t ev_attn[2] = {nullptr, nullptr}, ev_recv = nullptr, ev_start = nullptr;
+  // ring state, grown on demand
+  void* buf = nullptr;
+  size_t buf_bytes = 0;
+};
+
+namespace aex {
+namespace {
+
+int grow(aex_comm* c, size_t bytes) {
+  if (c->buf_bytes >= bytes) return AEX_OK;
+  if (c->buf) {
+    AEX_CUDA_TRY(c->ctx, cudaDeviceSynchronize());
+    cudaFree(c->buf);
+    c->buf = nullptr;
+    c->buf_bytes = 0;
+  }
+  AEX_CUDA_TRY(c->ctx, cudaMalloc(&c->buf, bytes));
+  c->buf_bytes = bytes;
+  return AEX_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace aex
+
+extern "C" {
+
+int aex_comm_unique_id(void* id_out) {
+  using namespace aex;
+  if (!id_out) return set_error(nullptr, AEX_ERR_INVALID_ARG, "NULL id");
+  if (!nccl().ok) return set_error(nullptr, AEX_ERR_NCCL, "NCCL library not found (libnccl.so.2)");
+  ncclUniqueId id;
+  ncclResult_t r = nccl().getUniqueId(&id);
+  if (r != ncclSuccess) return nccl_error(nullptr, r, "ncclGetUniqueId");
+  static_assert(sizeof(ncclUniqueId) == AEX_COMM_ID_BYTES, "unique id size");
+  std::memcpy(id_out, &id, sizeof id);
+  return AEX_OK;
+}
+
+int aex_comm_create(aex_ctx* ctx, int world, int rank, const void* id, int timeout_ms, aex_comm** out) {
+  using namespace aex;
+  if (!ctx || !id || !out) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  if (world < 1 || rank < 0 || rank >= world) return set_error(ctx, AEX_ERR_INVALID_ARG, "bad world/rank");
+  if (!nccl().ok) return set_error(ctx, AEX_ERR_NCCL, "NCCL library not found (libnccl.so.2)");
+  if (int r = bind_device(ctx)) return r;
+  auto* c = new aex_comm();
+  c->ctx = ctx;
+  c->world = world;
+  c->rank = rank;
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof uid);
+  // Non-blocking init, polled with a deadline, so a missing peer cannot hang the caller.
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = nccl().commInitRankConfig(&c->comm, world, uid, rank, &cfg);
+  const auto t0 = std::chrono::steady_clock::now();
+  ncclResult_t st = ncclInProgress;
+  while (r == ncclSuccess || r == ncclInProgress) {
+    r = nccl().commGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess || st != ncclInProgress) break;
+    if (timeout_ms > 0 && std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      nccl().commAbort(c->comm);
+      delete c;
+      return set_error(ctx, AEX_ERR_TIMEOUT, "NCCL communicator init did not complete in %d ms", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  }
+  if (r != ncclSuccess || st != ncclSuccess) {
+    if (c->comm) nccl().commAbort(c->comm);
+    delete c;
+    return nccl_error(ctx, r != ncclSuccess ? r : st, "ncclCommInitRankConfig");
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&c->ev_attn[i], cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_recv, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    aex_comm_destroy(c);
+    return cuda_error(ctx, e, "stream/event creation");
+  }
+  *out = c;
+  return AEX_OK;
+}
+
+void aex_comm_destroy(aex_comm* c) {
+  using namespace aex;
+  if (!c) return;
+  cudaSetDevice(c->ctx->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->comm) nccl().commDestroy(c->comm);
+  for (auto* ev : {c->ev_attn[0], c->ev_attn[1], c->ev_recv, c->ev_start})
+    if (ev) cudaEventDestroy(ev);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->buf) cudaFree(c->buf);
+  delete c;
+}
+
+int aex_comm_abort(aex_comm* c) {
+  using namespace aex;
+  if (!c || !c->comm) return AEX_ERR_INVALID_ARG;
+  ncclResult_t r = nccl().commAbort(c->comm);
+  c->comm = nullptr;
+  return r == ncclSuccess ? AEX_OK : AEX_ERR_NCCL;
+}
+
+int aex_ring_attention(aex_ctx* ctx, aex_comm* c, const aex_attention_args* a, aex_stream stream) {
+  using namespace aex;
+  if (!ctx || !c || !a) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL argument");
+  if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
+  if (a->head_dim != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "head_dim must be 128");
+  if (a->batch != 1) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention takes batch 1");
+  if (a->seq <= 0 || a->heads <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "seq/heads must be positive");
+  if (int r = bind_device(ctx)) return r;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int P = c->world, r = c->rank, S = a->seq, H = a->heads;
+  const size_t plane = static_cast<size_t>(H) * S * 128;  // elements of one [H][S][128] or [S][H][128] block
+  // Layout of the ring state: Q plane | K ring[2] (head-major) | V ring[2] (token-major) |
+  // O_h bf16 | O_acc f32 | lse_h | lse ping-pong[2].
+  const size_t bq = align256(plane * 2), bkv = align256(plane * 2), bo = align256(plane * 2),
+               bacc = align256(plane * 4), blse = align256(static_cast<size_t>(H) * S * 4);
+  const size_t off_q = 0, off_k = bq, off_v = off_k + 2 * bkv, off_o = off_v + 2 * bkv, off_acc = off_o + bo,
+               off_lh = off_acc + bacc, off_l0 = off_lh + blse, total = off_l0 + 2 * blse;
+  if (int e = grow(c, total)) return e;
+  uint8_t* base = static_cast<uint8_t*>(c->buf);
+  uint16_t* Q = reinterpret_cast<uint16_t*>(base + off_q);
+  uint16_t* Kr[2] = {reinterpret_cast<uint16_t*>(base + off_k), reinterpret_cast<uint16_t*>(base + off_k + bkv)};
+  uint16_t* Vr[2] = {reinterpret_cast<uint16_t*>(base + off_v), reinterpret_cast<uint16_t*>(base + off_v + bkv)};
+  uint16_t* Oh = reinterpret_cast<uint16_t*>(base + off_o);
+  float* Oacc = reinterpret_cast<float*>(base + off_acc);
+  float* lse_h = reinterpret_cast<float*>(base + off_lh);
+  float* lse_acc[2] = {reinterpret_cast<float*>(base + off_l0), reinterpret_cast<float*>(base + off_l0 + blse)};
+  // 1. This rank's Q and K: norm + RoPE (rows of the local shard) straight into Q and K ring[0]
+  //    (the prep writes the Q plane, then the K plane, contiguously; K ring[0] follows Q).
+  const int64_t qs[3] = {a->q.stride_b, a->q.stride_s, a->q.stride_h};
+  const int64_t ks[3] = {a->k.stride_b, a->k.stride_s, a->k.stride_h};
+  if (bq != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
+  if (int e = launch_qk_prep(ctx, a->q.data, qs, a->k.data, ks, 1, S, H, a->norm_q_weight, a->norm_k_weight, nullptr,
+                             nullptr, 0, a->eps, a->rope_cos, a->rope_sin, Q, s))
+    return e;
+  // 2. This rank's V into V ring[0] (token-major, contiguous rows of H*128).
+  AEX_CUDA_TRY(ctx, cudaMemcpy2DAsync(Vr[0], static_cast<size_t>(H) * 256, a->v.data,
+                                      static_cast<size_t>(a->v.stride_s) * 2, static_cast<size_t>(H) * 256, S,
+                                      cudaMemcpyDeviceToDevice, s));
+  if (a->v.stride_h != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention needs V heads contiguous");
+  AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_start, s));
+  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_start, 0));
+  const int64_t q_st[3] = {static_cast<int64_t>(plane), 128, static_cast<int64_t>(S) * 128};   // head-major
+  const int64_t v_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};  // token-major
+  const int64_t o_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};
+  const size_t kv_bytes = plane * 2;
+  const int next = (r + 1) % P, prev = (r - 1 + P) % P;
+  for (int hop = 0; hop < P; ++hop) {
+    const int cur = hop & 1, nxt = cur ^ 1;
+    if (hop + 1 < P) {
+      // Exchange on the ring stream: send the shard in hand, receive the next one.
+      if (hop > 0) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_attn[nxt], 0));  // nxt no longer read
+      ncclResult_t nr = nccl().groupStart();
+      if (nr == ncclSuccess) nr = nccl().send(Kr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
+      if (nr == ncclSuccess) nr = nccl().send(Vr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
+      if (nr == ncclSuccess) nr = nccl().recv(Kr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
+      if (nr == ncclSuccess) nr = nccl().recv(Vr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
+      ncclResult_t ne = nccl().groupEnd();
+      if (nr != ncclSuccess && nr != ncclInProgress) return nccl_error(ctx, nr, "ncclSend/ncclRecv");
+      // Non-blocking communicator: wait (bounded) until the group is enqueued on the stream.
+      const auto t0 = std::chrono::steady_clock::now();
+      while (ne == ncclInProgress) {
+        ncclResult_t st = ncclInProgress;
+        const ncclResult_t q = nccl().commGetAsyncError(c->comm, &st);
+        if (q != ncclSuccess) return nccl_error(ctx, q, "ncclCommGetAsyncError");
+        ne = st;
+        if (ne == ncclInProgress && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30))
+          return set_error(ctx, AEX_ERR_TIMEOUT, "NCCL group not enqueued after 30 s");
+      }
+      if (ne != ncclSuccess) return nccl_error(ctx, ne, "ncclGroupEnd");
+      AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_recv, c->stream));
+    }
+    // Attention of the local queries against the shard in hand, then merge.
+    if (int e = launch_attention_core(ctx, Q, q_st, Kr[cur], q_st, Vr[cur], v_st, Oh, o_st, 1, S, S, H, a->scale,
+                                      lse_h, 0, S, s))
+      return e;
+    AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_attn[cur], s));
+    if (int e = ring::merge(ctx, Oh, static_cast<int64_t>(H) * 128, 128, lse_h, lse_acc[hop & 1],
+                            lse_acc[(hop + 1) & 1], Oacc, S, H, hop == 0, hop == P - 1, a->out.data, a->out.stride_s,
+                            a->out.stride_h, s))
+      return e;
+    if (hop + 1 < P) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(s, c->ev_recv, 0));
+  }
+  return AEX_OK;
+}
+
+}  // extern "C"

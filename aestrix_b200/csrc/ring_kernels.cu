@@ -1,0 +1,72 @@
+// ring_kernels.cu — merging partial attention results of different K/V shards
+// (the ring-attention accumulation step). Each hop's attention kernel writes a
+// normalized partial output O_h (bf16) and its per-row log2-sum-exp lse_h; the
+// running result is
+//   lse = log2(2^lse_acc + 2^lse_h),
+//   O   = (2^(lse_acc - lse) O_acc + 2^(lse_h - lse) O_h),
+// i.e. the online-softmax rescaling of FlashAttention applied across shards.
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace aex {
+namespace ring {
+namespace {
+
+// One thread per (token s, head h, 8 columns).
+__global__ void merge_kernel(const uint16_t* __restrict__ o_h, int64_t oh_ss, int64_t oh_sh,
+                             const float* __restrict__ lse_h, const float* __restrict__ lse_in,
+                             float* __restrict__ lse_out, float* __restrict__ o_acc, int S, int H, int first, int final,
+                             uint16_t* __restrict__ out, int64_t out_ss, int64_t out_sh) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(S) * H * 16) return;
+  const int c = static_cast<int>(idx & 15);
+  const int64_t sh = idx >> 4;
+  const int h = static_cast<int>(sh % H);
+  const int s = static_cast<int>(sh / H);
+  const float lh = lse_h[static_cast<int64_t>(h) * S + s];
+  const uint4 raw = *reinterpret_cast<const uint4*>(o_h + s * oh_ss + h * oh_sh + c * 8);
+  const uint32_t rv[4] = {raw.x, raw.y, raw.z, raw.w};
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf16lo_to_f32(rv[i]);
+    v[2 * i + 1] = bf16hi_to_f32(rv[i]);
+  }
+  float* acc = o_acc + (static_cast<int64_t>(s) * H + h) * 128 + c * 8;
+  float lse_new = lh;
+  if (!first) {
+    const float la = lse_in[static_cast<int64_t>(h) * S + s];
+    const float mx = fmaxf(la, lh);
+    const float wa = exp2f(la - mx), wh = exp2f(lh - mx);
+    const float inv = 1.f / (wa + wh);
+    lse_new = mx + log2f(wa + wh);
+    const float4 a0 = *reinterpret_cast<const float4*>(acc);
+    const float4 a1 = *reinterpret_cast<const float4*>(acc + 4);
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (av[i] * wa + v[i] * wh) * inv;
+  }
+  if (final) {
+    *reinterpret_cast<uint4*>(out + s * out_ss + h * out_sh + c * 8) =
+        make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  } else {
+    *reinterpret_cast<float4*>(acc) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(acc + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    if (c == 0) lse_out[static_cast<int64_t>(h) * S + s] = lse_new;
+  }
+}
+
+}  // namespace
+
+int merge(aex_ctx* ctx, const void* o_h, int64_t oh_ss, int64_t oh_sh, const float* lse_h, const float* lse_in,
+          float* lse_out, float* o_acc, int S, int H, bool first, bool final, void* out, int64_t out_ss, int64_t out_sh,
+          cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(S) * H * 16;
+  merge_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+      static_cast<const uint16_t*>(o_h), oh_ss, oh_sh, lse_h, lse_in, lse_out, o_acc, S, H, first ? 1 : 0,
+      final ? 1 : 0, static_cast<uint16_t*>(out), out_ss, out_sh);
+  return check_launch(ctx, "ring merge_kernel");
+}
+
+}  // namespace ring
+}  // namespace aex

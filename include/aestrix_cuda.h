@@ -257,6 +257,29 @@ int aex_dit_denoise_step(aex_dit* dit, const float* lat_in, float* lat_out, floa
  * the result on return (DirectDiTPackedDenoiser.denoise :25-81). */
 int aex_dit_denoise(aex_dit* dit, float* latents, int steps, aex_stream stream);
 
+/* ------------------------------------------------ multi-GPU (NCCL, NVLink) */
+
+/* Sequence-parallel ring attention over P GPUs, one process per GPU. No
+ * counterpart exists in the single-device reference, which keeps the full
+ * sequence on one device (ParallelSelfAttention.swift:134-136); this computes
+ * the same softmax(scale*QK^T)V for the 2048^2 joint sequence (512 text +
+ * 16384 image tokens) split into P equal contiguous shards. NCCL is resolved
+ * at run time (libnccl.so.2 or the copy already loaded in the process). */
+typedef struct aex_comm aex_comm;
+#define AEX_COMM_ID_BYTES 128
+
+/* 128-byte NCCL unique id, created on one rank and shared with the others. */
+int aex_comm_unique_id(void* id_out);
+/* Collective over `world` ranks; gives up after timeout_ms (<= 0: no bound). */
+int aex_comm_create(aex_ctx* ctx, int world, int rank, const void* id, int timeout_ms, aex_comm** out);
+void aex_comm_destroy(aex_comm* comm);
+/* Abort in-flight NCCL work of this communicator (after a failed/timed-out sync). */
+int aex_comm_abort(aex_comm* comm);
+/* args describe this rank's shard: batch 1, seq = shard length (equal on all
+ * ranks), the norm weights and the RoPE rows of the shard's tokens; V heads
+ * contiguous. Every rank calls it with the same shapes. */
+int aex_ring_attention(aex_ctx* ctx, aex_comm* comm, const aex_attention_args* args, aex_stream stream);
+
 /* -------------------------------------------------------------- self test */
 
 /* Tensor-core path self test (no reference counterpart; a device bring-up
