@@ -31,6 +31,8 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# stdout carries exactly one JSON line: keep NCCL's own log lines on stderr.
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 import numpy as np  # noqa: E402
 
@@ -343,6 +345,60 @@ def measure_dit(ctx, dev, world, runs=3):
             "config": "BASELINE configs[3]: FLUX.2-klein 1024^2, 4 steps, random-init 4-bit weights, 1 image/GPU"}
 
 
+def measure_ring(ctx, dev, world, rank, iters=5):
+    """joint attention at 2048^2 (512 text + 16384 image tokens = 16896, 24 x 128,
+    bf16, fused QK-RMSNorm + RoPE), sequence-parallel ring attention over the N GPUs (contiguous shards,
+    K/V exchanged with NCCL over NVLink and overlapped with compute). Device time, max over ranks;
+    TFLOP/s counts the whole call's 4*S^2*D*H."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from aestrix_b200 import _lib, attention
+
+    S, H = 512 + 128 * 128, HEADS
+    if S % world:
+        return {"skipped": f"sequence {S} not divisible by {world}"}
+    Sp = S // world
+    L = _lib.lib()
+    uid = (C.c_char * 128)()
+    if rank == 0:
+        ctx.check(L.aex_comm_unique_id(uid))
+    t = torch.frombuffer(bytearray(bytes(uid)), dtype=torch.uint8).to(dev)
+    dist.broadcast(t, src=0)
+    uid = (C.c_char * 128).from_buffer_copy(bytes(t.cpu().numpy()))
+    comm = C.c_void_p()
+    ctx.check(L.aex_comm_create(ctx.handle, world, rank, uid, 120000, C.byref(comm)))
+    g = torch.Generator().manual_seed(77 + rank)
+    q, k, v = (torch.randn(1, Sp, H, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    wk = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    ang = torch.rand(Sp, 64, generator=g) * 6.2831853
+    cos, sin = torch.cos(ang).to(dev), torch.sin(ang).to(dev)
+    out = torch.empty_like(q)
+    a = attention.make_args(q, k, v, out, "bshd", wq, wk, 1e-6, cos, sin)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(2):
+        ctx.check(L.aex_ring_attention(ctx.handle, comm, C.byref(a), stream.cuda_stream))
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        ctx.check(L.aex_ring_attention(ctx.handle, comm, C.byref(a), stream.cuda_stream))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(world, e0.elapsed_time(e1) / iters)
+    ctx.sync(stream.cuda_stream)
+    L.aex_comm_destroy(comm)
+    flops = 4.0 * S * S * HEAD_DIM * H
+    kv_bytes_per_hop = 2 * Sp * H * HEAD_DIM * 2
+    return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "gflop_per_call": flops / 1e9, "seq": S,
+            "shard": Sp, "hops": world, "kv_bytes_per_hop": kv_bytes_per_hop,
+            "config": "BASELINE configs[4]: 2048^2 joint attention, sequence-parallel ring over NCCL"}
+
+
 def run_ours(args):
     import torch
 
@@ -440,6 +496,7 @@ def run_ours(args):
 
     qmm_res = measure_qmm(ctx, dev) if not args.no_qmm else None
     dit_res = measure_dit(ctx, dev, world) if not args.no_dit else None
+    ring_res = measure_ring(ctx, dev, world, rank) if (world > 1 and not args.no_ring) else None
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = FLOPS_PER_CALL / (kernel_ms * 1e-3) / 1e12
@@ -464,6 +521,8 @@ def run_ours(args):
         }
         if dit_res is not None:
             line["dit_denoise"] = dit_res
+        if ring_res is not None:
+            line["ring_attention_2048"] = ring_res
         if qmm_res is not None:
             hbm = _hbm_peak()
             for v in qmm_res.values():
@@ -488,6 +547,7 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target duration of the reference arm")
     ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 4-step DiT denoise measurement")
+    ap.add_argument("--no-ring", action="store_true", help="skip the 2048^2 ring attention measurement (N > 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
