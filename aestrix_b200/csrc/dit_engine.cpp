@@ -187,27 +187,28 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + C, mt, eps_ln, NHt, C, s));
   AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + C, mi, eps_ln, NHi, C, s));
   const int64_t pq = 3 * C;  // PROJ row pitch for Q|K|V
-  AEX_TRY(qmm_run(d->ctx, qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr, s));
+  // Each text-stream linear shares one launch with its image-stream twin.
+  AEX_TRY(qmm_run2(d->ctx, QmmJob{qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr},
+                   QmmJob{qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr}, s));
   const int64_t qs[3] = {static_cast<int64_t>(J) * pq, pq, 128};
   AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, d->H, nq, nk, naq, nak, lt, d->cfg.rms_eps, d->COS,
                          d->SIN, d->PREP, s));
   AEX_TRY(attend(d, d->PROJ + 2 * C, pq, d->ATT, C, s));
-  AEX_TRY(qmm_run(d->ctx, out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C, s));
-  AEX_TRY(qmm_run(d->ctx, out_i, d->ATT + static_cast<int64_t>(lt) * C, C, li, Xi, C, 2, mi + 2 * C, s));
+  AEX_TRY(qmm_run2(d->ctx, QmmJob{out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C},
+                   QmmJob{out_i, d->ATT + static_cast<int64_t>(lt) * C, C, li, Xi, C, 2, mi + 2 * C}, s));
   // MLP half (per stream)
   AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + 4 * C, mt + 3 * C, eps_ln, NHt, C, s));
   AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + 4 * C, mi + 3 * C, eps_ln, NHi, C, s));
   const int64_t pf = 2 * mlp;
   uint16_t* SWt = d->ATT;                                   // [lt, mlp]
   uint16_t* SWi = d->ATT + static_cast<int64_t>(lt) * mlp;  // [li, mlp]
-  AEX_TRY(qmm_run(d->ctx, ffi_t, NHt, C, lt, d->PROJ, pf, 0, nullptr, s));
-  AEX_TRY(glue::swiglu(d->ctx, d->PROJ, d->PROJ + mlp, pf, lt, mlp, SWt, mlp, s));
-  AEX_TRY(qmm_run(d->ctx, ffo_t, SWt, mlp, lt, Xt, C, 2, mt + 5 * C, s));
   uint16_t* Pi = d->PROJ + static_cast<int64_t>(lt) * pf;
-  AEX_TRY(qmm_run(d->ctx, ffi_i, NHi, C, li, Pi, pf, 0, nullptr, s));
-  AEX_TRY(glue::swiglu(d->ctx, Pi, Pi + mlp, pf, li, mlp, SWi, mlp, s));
-  AEX_TRY(qmm_run(d->ctx, ffo_i, SWi, mlp, li, Xi, C, 2, mi + 5 * C, s));
+  AEX_TRY(qmm_run2(d->ctx, QmmJob{ffi_t, NHt, C, lt, d->PROJ, pf, 0, nullptr},
+                   QmmJob{ffi_i, NHi, C, li, Pi, pf, 0, nullptr}, s));
+  // Text rows then image rows are contiguous in PROJ and in SW: one SwiGLU over all J rows.
+  AEX_TRY(glue::swiglu(d->ctx, d->PROJ, d->PROJ + mlp, pf, J, mlp, SWt, mlp, s));
+  AEX_TRY(qmm_run2(d->ctx, QmmJob{ffo_t, SWt, mlp, lt, Xt, C, 2, mt + 5 * C},
+                   QmmJob{ffo_i, SWi, mlp, li, Xi, C, 2, mi + 5 * C}, s));
   return AEX_OK;
 }
 

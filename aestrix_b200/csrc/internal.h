@@ -18,6 +18,7 @@ struct aex_ctx {
   int* d_status = nullptr;  // device status word written by kernels on a bounded-wait expiry
   void* scratch = nullptr;  // grown on demand by entry points that need workspace
   size_t scratch_bytes = 0;
+  int pair_clusters = 0;    // co-resident 2-CTA clusters of the pair GEMM (0 = not yet queried)
   std::string last_error;
 };
 
@@ -62,6 +63,19 @@ int check_launch(aex_ctx* ctx, const char* what);
 // (y_f32[row, col] += gate[col] * acc). No argument validation beyond m/gate.
 int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy, int mode,
             const float* gate, cudaStream_t s);
+// Up to two independent linears in one launch where both take the GEMM path
+// (the text and image streams of a double block); otherwise one after the other.
+struct QmmJob {
+  const aex_qweight* w;
+  const void* x;
+  int64_t ldx;
+  int m;
+  void* y;
+  int64_t ldy;
+  int mode;
+  const float* gate;
+};
+int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s);
 // QK-RMSNorm + RoPE pre-pass into head-major scratch [2][B][H][S][128]; tokens
 // s < split use (wq_a, wk_a), the others (wq, wk).
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,

@@ -11,17 +11,18 @@
 //
 // K0  unpack_kernel — MLX layout (packed uint32 [n, k/8], LSB-first nibbles;
 //     bf16 scales/biases [n, k/64]) -> tile layout: for every 256-row tile `nt`
-//     and 64-wide K block `kb` one contiguous 9216-byte chunk
-//        [0, 8192)     row r's 32 packed bytes at r*32 (the MLX words, unchanged)
-//        [8192, 8704)  bf16 scale of row r at 8192 + 2r
-//        [8704, 9216)  bf16 bias  of row r at 8704 + 2r
+//     and 64-wide K block `kb` one contiguous 9216-byte chunk made of two
+//     4608-byte halves (rows 0-127, rows 128-255); in half h, for row r = 128h + i
+//        [0, 4096)     row r's 32 packed bytes at 32i (the MLX words, unchanged)
+//        [4096, 4352)  bf16 scale of row r at 4096 + 2i
+//        [4352, 4608)  bf16 bias  of row r at 4352 + 2i
 //     chunk (nt, kb) at byte (nt * k_blocks + kb) * 9216; rows past n are zero.
-//     One bulk copy moves one chunk into shared memory.
-// K2  gemm_kernel<MT> — tcgen05 GEMM, CTA tile (128*MT) x 256 x 64-wide K steps:
-//     warp 0 TMA producer (x tile) + bulk copy (packed chunk), warp 1 UMMA
-//     issuer, warps 4..19 dequantize the chunk in registers into the 128-byte
-//     swizzled K-major bf16 B tile and, after the main loop, drain the f32
-//     accumulators from tensor memory (epilogue).
+//     One bulk copy moves one chunk (or, in the CTA-pair GEMM, one half) into
+//     shared memory.
+// K2  gemm_pair_kernel — tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256
+//     output tiles, persistent over up to two problems per launch; the
+//     weights are dequantized in registers into the 128-byte swizzled K-major
+//     bf16 B tile (see the kernel's comment for the roles and the pipeline).
 //     gemv_kernel<R> — R <= 16 activation rows, HBM-bound: one thread per
 //     weight row, split-K over a thread-block cluster, partial sums reduced
 //     through distributed shared memory (no scratch, no atomics). The dot uses
@@ -37,13 +38,75 @@ namespace qmm {
 
 constexpr int kTileN = 256;
 constexpr int kKB = 64;
-constexpr int kChunkPacked = kTileN * 32;
-constexpr int kChunkBytes = kChunkPacked + kTileN * 4;  // + bf16 scales + bf16 biases
-constexpr int kOffScale = kChunkPacked;
-constexpr int kOffBias = kChunkPacked + kTileN * 2;
+constexpr int kHalfBytes = 128 * 36;  // 128 rows x (32 packed bytes + bf16 scale + bf16 bias)
+constexpr int kChunkBytes = 2 * kHalfBytes;
+
+// Byte offsets of row r (0..255) inside a chunk.
+__host__ __device__ constexpr int pk_off(int r) { return (r >> 7) * kHalfBytes + (r & 127) * 32; }
+__host__ __device__ constexpr int sc_off(int r) { return (r >> 7) * kHalfBytes + 4096 + (r & 127) * 2; }
+__host__ __device__ constexpr int bi_off(int r) { return (r >> 7) * kHalfBytes + 4352 + (r & 127) * 2; }
 
 __host__ __device__ inline size_t chunk_offset(int nt, int kb, int k_blocks) {
   return (static_cast<size_t>(nt) * k_blocks + kb) * kChunkBytes;
+}
+
+// The tile layout stores each packed word with its nibbles permuted: nibble i
+// (bits 4i..4i+3) holds code 2i for i < 4 and code 2(i-4)+1 for i >= 4, so
+// that (w >> 4j) & 0x000F000F puts codes (2j, 2j+1) in the two 16-bit halves.
+__host__ __device__ __forceinline__ uint32_t nibble_compress(uint32_t x) {  // 4 bytes < 16 -> 4 nibbles
+  x = (x | (x >> 4)) & 0x00FF00FFu;
+  return (x | (x >> 8)) & 0x0000FFFFu;
+}
+__host__ __device__ __forceinline__ uint32_t permute_word(uint32_t w) {
+  return nibble_compress(w & 0x0F0F0F0Fu) | (nibble_compress((w >> 4) & 0x0F0F0F0Fu) << 16);
+}
+
+// Codes (2j, 2j+1) of a permuted word as a bf16 pair (128 + q): 0x4300 is
+// bf16 128.0 and the code lands in the low mantissa bits.
+__device__ __forceinline__ uint32_t code_pair_128(uint32_t wp, int j) {
+  return ((wp >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+}
+
+// Exact dequant of a permuted word (the reference's f32 scale*q + bias, then
+// RNE to bf16), 8 bf16 in K order.
+__device__ __forceinline__ uint4 dequant_word_exact(uint32_t wp, float s, float b) {
+  uint32_t out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t t = code_pair_128(wp, j);
+    const float2 q = fadd2(make_float2(__uint_as_float(t << 16), __uint_as_float(t & 0xFFFF0000u)),
+                           make_float2(-128.0f, -128.0f));
+    const float2 v = ffma2(q, make_float2(s, s), make_float2(b, b));
+    out[j] = pack_bf16x2(v.x, v.y);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// True when f32(scale * q + bias) is exact for every code q in 0..15, so that
+// one bf16 rounding of the exact value (a bf16 fma) equals the reference's
+// f32-then-bf16 rounding. scale * q is a multiple of 2^(Es-7) below 2^(Es+5),
+// bias a multiple of 2^(Eb-7) below 2^(Eb+1); their sum fits a 24-bit
+// significand when max(Es+5, Eb+1) - min(Es, Eb) <= 16. Zeros are exact;
+// subnormals, infinities and NaN take the f32 path.
+__device__ __forceinline__ bool one_rounding_exact(uint32_t s16, uint32_t b16) {
+  if ((s16 & 0x7FFFu) == 0 || (b16 & 0x7FFFu) == 0) return true;
+  const int es = static_cast<int>((s16 >> 7) & 0xFFu), eb = static_cast<int>((b16 >> 7) & 0xFFu);
+  if (es == 0 || eb == 0 || es == 0xFF || eb == 0xFF) return false;
+  return max(es + 5, eb + 1) - min(es, eb) <= 16;
+}
+
+// Fast dequant of a permuted word: exact codes (128 + q) - 128 in bf16, then
+// one fma.rn.bf16x2 (q * scale + bias, rounded once). Bit-exact with the
+// reference when one_rounding_exact(scale, bias).
+__device__ __forceinline__ uint4 dequant_word_fast(uint32_t wp, uint32_t s2, uint32_t b2) {
+  uint32_t out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t q;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(code_pair_128(wp, j)), "r"(0x43004300u));
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(out[j]) : "r"(q), "r"(s2), "r"(b2));
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 // ------------------------------------------------------------------ K0 unpack
@@ -60,14 +123,16 @@ __global__ void __launch_bounds__(256) unpack_kernel(const uint32_t* __restrict_
     const uint4* src = reinterpret_cast<const uint4*>(packed + (static_cast<size_t>(row) * k_blocks + kb) * 8);
     a = src[0];
     b = src[1];
+    a = make_uint4(permute_word(a.x), permute_word(a.y), permute_word(a.z), permute_word(a.w));
+    b = make_uint4(permute_word(b.x), permute_word(b.y), permute_word(b.z), permute_word(b.w));
     s = scales[static_cast<size_t>(row) * k_blocks + kb];
     bi = biases[static_cast<size_t>(row) * k_blocks + kb];
   }
-  uint4* dst = reinterpret_cast<uint4*>(chunk + r * 32);
+  uint4* dst = reinterpret_cast<uint4*>(chunk + pk_off(r));
   dst[0] = a;
   dst[1] = b;
-  reinterpret_cast<uint16_t*>(chunk + kOffScale)[r] = s;
-  reinterpret_cast<uint16_t*>(chunk + kOffBias)[r] = bi;
+  *reinterpret_cast<uint16_t*>(chunk + sc_off(r)) = s;
+  *reinterpret_cast<uint16_t*>(chunk + bi_off(r)) = bi;
 }
 
 // Dequantize one packed word (8 codes of one row) to 8 bf16 values, bit-exact
@@ -90,6 +155,7 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, float s, float b) {
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t u) { return __uint_as_float(static_cast<uint32_t>(u) << 16); }
 
+
 // Tile layout (or MLX layout) -> row-major bf16 [n, k]; one thread per word.
 __global__ void __launch_bounds__(256) dequant_tiles_kernel(const uint8_t* __restrict__ tiles, int n, int k_blocks,
                                                             uint16_t* __restrict__ out) {
@@ -101,10 +167,10 @@ __global__ void __launch_bounds__(256) dequant_tiles_kernel(const uint8_t* __res
   const int kb = rem >> 3, c = rem & 7;
   const uint8_t* chunk = tiles + chunk_offset(row / kTileN, kb, k_blocks);
   const int r = row % kTileN;
-  const uint32_t w = *reinterpret_cast<const uint32_t*>(chunk + r * 32 + c * 4);
-  const float s = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(chunk + kOffScale)[r]);
-  const float b = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(chunk + kOffBias)[r]);
-  *reinterpret_cast<uint4*>(out + wi * 8) = dequant_word(w, s, b);
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(chunk + pk_off(r) + c * 4);
+  const float s = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(chunk + sc_off(r)));
+  const float b = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(chunk + bi_off(r)));
+  *reinterpret_cast<uint4*>(out + wi * 8) = dequant_word_exact(w, s, b);
 }
 
 __global__ void __launch_bounds__(256) dequant_mlx_kernel(const uint32_t* __restrict__ packed,
@@ -120,230 +186,380 @@ __global__ void __launch_bounds__(256) dequant_mlx_kernel(const uint32_t* __rest
   *reinterpret_cast<uint4*>(out + wi * 8) = dequant_word(packed[wi], s, b);
 }
 
-// ------------------------------------------------------------------ K2 GEMM
+// Epilogue modes of the GEMM and GEMV kernels.
 enum OutMode : int { kOutBf16 = 0, kOutF32 = 1, kOutResidualGate = 2 };
 
-constexpr int kGemmThreads = 640;  // warps 0 producer, 1 UMMA, 2-3 idle, 4-19 dequant + epilogue
-constexpr int kDequantWarp0 = 4;
-constexpr int kDequantThreads = 512;  // one half-row (4 packed words, 32 codes) per thread per K block
-constexpr int kGemmStages = 3;
-constexpr uint32_t kIdescGemm = idesc_bf16_f32(128, 256, false, false);
+// ------------------------------------------------------------------ K2 CTA-pair GEMM
+// Two CTAs of a cluster compute one 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256): CTA r holds x rows [128r, 128r + 128) of
+// the tile (A, by TMA) and dequantizes weight rows [128r, 128r + 128) of the
+// N-tile (its half of B, from its half of the chunk), and receives the f32
+// accumulators of its 128 x rows for all 256 columns in its tensor memory. Per
+// SM the tensor core reads 8 KB of shared memory per 128-cycle MMA instead of
+// 12 KB for a one-CTA 128 x 256 MMA.
+// Persistent: cluster c walks tiles c, c + clusters, ...; a tile index covers
+// up to two problems (same kernel, different x / weights / outputs) so that a
+// short problem (text rows) shares the launch with a long one. Two 256-column
+// accumulator buffers let the epilogue of one tile overlap the main loop of
+// the next.
+//   warp 0      producer: TMA of the A box + bulk copy of the chunk half
+//   warp 1      UMMA issuer (even CTA only)
+//   warp 2      tensor-memory allocation
+//   warps 4-7   epilogue (tensor-memory lane quadrant = warp % 4)
+//   warps 8-    dequantize: kPairGroups groups of warps take turns over the K
+//               blocks; within a group each thread converts 8 / kPairSplit
+//               packed words of one row per K block.
+// Synchronisation per K block (stage s): the producers' TMA + bulk copy land on
+// each CTA's full[s]; each dequant warp of either CTA arrives on the even CTA's
+// bready[s] (count: both CTAs' warps of one group); the UMMA thread waits on
+// bready[s], issues 4 MMAs and commits once to the even CTA's empty[s], whose
+// producer forwards the completion to the odd CTA's empty[s]. Measured on B200:
+// remote arrives use the default CTA-scope release (a cluster-scope release
+// cost ~1000 cycles per arrive), and the UMMA loop is kept short (one commit,
+// stage and phase advanced incrementally) because the tensor core's queue of
+// pending MMAs is short: cycles the issuing thread spends between MMAs idle it.
+#ifndef AEX_PAIR_GROUPS
+#define AEX_PAIR_GROUPS 2
+#endif
+#ifndef AEX_PAIR_SPLIT
+#define AEX_PAIR_SPLIT 1
+#endif
+constexpr int kPairGroups = AEX_PAIR_GROUPS;
+constexpr int kPairSplit = AEX_PAIR_SPLIT;                // threads per row (1, 2 or 4)
+static_assert(kPairSplit == 1 || kPairSplit == 2 || kPairSplit == 4, "AEX_PAIR_SPLIT must be 1, 2 or 4");
+constexpr int kPairWords = 8 / kPairSplit;                // packed words per thread per K block
+constexpr int kPairDeqWarps = 4 * kPairSplit;             // dequant warps per group
+constexpr int kPairThreads = 32 * (8 + kPairGroups * kPairDeqWarps);
+constexpr int kPairEpi0 = 4;
+constexpr int kPairDeq0 = 8;
+constexpr int kPairStages = 6;
+constexpr int kPairABytes = 128 * kKB * 2;
+constexpr int kPairBBytes = 128 * kKB * 2;
+constexpr int kPairOffB = kPairABytes;
+constexpr int kPairOffPk = kPairABytes + kPairBBytes;
+constexpr int kPairStage = (kPairOffPk + kHalfBytes + 1023) & ~1023;
+constexpr int kPairOffBar = kPairStages * kPairStage;
+// bars: full[S], bready[S], empty[S], accf[2], acce[2], drain
+constexpr int kPairNumBars = 3 * kPairStages + 5;
+constexpr int kPairSmem = kPairOffBar + kPairNumBars * 8 + 16 + 1024;
+static_assert(kPairSmem <= 232448, "pair GEMM exceeds the shared-memory limit");
+constexpr uint32_t kIdescPair = idesc_bf16_f32(256, 256, false, false);
+constexpr int kPairMaxProblems = 2;
 
-template <int MT>
-struct GemmLayout {
-  static constexpr int kABytes = MT * 128 * kKB * 2;  // MT boxes of 128 rows x 64 (16 KB each)
-  static constexpr int kBBytes = kTileN * kKB * 2;    // 32 KB dequantized B tile
-  static constexpr int kStageBytes = kABytes + kBBytes + kChunkBytes;
-  static constexpr int kOffA = 0;
-  static constexpr int kOffB = kABytes;
-  static constexpr int kOffPk = kABytes + kBBytes;
-  static constexpr int kOffBar = kGemmStages * kStageBytes;
-  // bars: full[S], bready[S], empty[S], acc
-  static constexpr int kNumBars = 3 * kGemmStages + 1;
-  static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;
-  static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
-};
-
-struct GemmParams {
+struct PairProblem {
   const uint8_t* tiles;
   int m, n, k_blocks;
+  int m_tiles;  // 256-row tiles of x
+  int tile0;    // first global tile index of this problem
   void* y;
   int64_t ldy;
-  int mode;           // kOutBf16, kOutF32, kOutResidualGate
-  const float* gate;  // kOutResidualGate: y_f32[row, col] += gate[col] * acc
-  int vec;  // y base and row pitch are 16-byte aligned: full 32-column runs use 16-byte stores
+  int mode;
+  const float* gate;
+  int vec;
 };
 
-template <int MT>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tm_x, GemmParams p, int* status) {
-  using L = GemmLayout<MT>;
+struct PairParams {
+  PairProblem prob[kPairMaxProblems];
+  int n_prob;
+  int tiles;
+};
+
+struct PairTile {
+  int pi, mt, nt;
+};
+
+__device__ __forceinline__ PairTile pair_tile(const PairParams& p, int t) {
+  const int pi = (p.n_prob > 1 && t >= p.prob[1].tile0) ? 1 : 0;
+  const int lt = t - p.prob[pi].tile0;
+  return PairTile{pi, lt % p.prob[pi].m_tiles, lt / p.prob[pi].m_tiles};
+}
+
+// Writes 32 accumulator columns [col, col + 32) of one output row.
+__device__ __forceinline__ void store_run(const PairProblem& q, int row, int col, const uint32_t* r) {
+  if (q.mode == kOutResidualGate) {
+    // Gated residual (dd_gate_add, DirectDiTKernels.swift:208-221): y += gate * acc, f32.
+    float* yr = static_cast<float*>(q.y) + static_cast<int64_t>(row) * q.ldy + col;
+    if (q.vec && col + 32 <= q.n) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 g = __ldg(reinterpret_cast<const float4*>(q.gate + col + i));
+        float4 v = *reinterpret_cast<float4*>(yr + i);
+        v.x = fmaf(g.x, __uint_as_float(r[i]), v.x);
+        v.y = fmaf(g.y, __uint_as_float(r[i + 1]), v.y);
+        v.z = fmaf(g.z, __uint_as_float(r[i + 2]), v.z);
+        v.w = fmaf(g.w, __uint_as_float(r[i + 3]), v.w);
+        *reinterpret_cast<float4*>(yr + i) = v;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < q.n) yr[i] = fmaf(q.gate[col + i], __uint_as_float(r[i]), yr[i]);
+    }
+  } else if (q.mode == kOutF32) {
+    float* yr = static_cast<float*>(q.y) + static_cast<int64_t>(row) * q.ldy + col;
+    if (q.vec && col + 32 <= q.n) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(yr + i) = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                                                         __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < q.n) yr[i] = __uint_as_float(r[i]);
+    }
+  } else {
+    uint16_t* yr = static_cast<uint16_t*>(q.y) + static_cast<int64_t>(row) * q.ldy + col;
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    if (q.vec && col + 32 <= q.n) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<uint4*>(yr + 2 * i) = make_uint4(pk[i], pk[i + 1], pk[i + 2], pk[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < q.n) yr[i] = static_cast<uint16_t>((i & 1) ? (pk[i >> 1] >> 16) : (pk[i >> 1] & 0xFFFFu));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kPairThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x0, const __grid_constant__ CUtensorMap tm_x1,
+                     const __grid_constant__ PairParams p, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairOffBar);
   uint64_t* full = bars;
-  uint64_t* bready = bars + kGemmStages;
-  uint64_t* empty = bars + 2 * kGemmStages;
-  uint64_t* acc = bars + 3 * kGemmStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  uint64_t* bready = bars + kPairStages;
+  uint64_t* empty = bars + 2 * kPairStages;
+  uint64_t* accf = bars + 3 * kPairStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kPairNumBars);
   __shared__ int abort_flag;
 
   const int warp = static_cast<int>(warp_id_uniform());
   const int lane = static_cast<int>(lane_id());
-  const int nt = blockIdx.x;
-  const int m0 = blockIdx.y * 128 * MT;
-  const int KB = p.k_blocks;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int clusters = static_cast<int>(gridDim.x >> 1);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < kGemmStages; ++s) {
+    for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bready[s], kDequantThreads / 32);
+      mbar_init(&bready[s], 2 * kPairDeqWarps);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 2 * 4);
+    }
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, MT * 256);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
   }
-  if (warp == 0 && lane == 0) prefetch_tmap(&tm_x);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_x0);
+    if (p.n_prob > 1) prefetch_tmap(&tm_x1);
+  }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // barriers of both CTAs initialized, tensor memory allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer
-      int issued = 0;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kGemmStages, use = kb / kGemmStages;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, &abort_flag, status, kDevTimeoutTma)) break;
-        uint8_t* st = smem + s * L::kStageBytes;
-        mbar_arrive_expect_tx(&full[s], L::kABytes + kChunkBytes);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-          tma_load_2d(st + L::kOffA + mt * 16384, &tm_x, &full[s], kb * kKB, m0 + mt * 128);
-        bulk_load(st + L::kOffPk, p.tiles + chunk_offset(nt, kb, KB), kChunkBytes, &full[s]);
-        issued = kb + 1;
+      // Stage s and its phase bit advance together; the even CTA's producer
+      // also forwards each "stage free" completion (a tensor-core commit on
+      // its own empty barrier) to the odd CTA's empty barrier.
+      const uint32_t empty0 = smem_u32(&empty[0]);
+      const uint32_t peer_empty0 = mapa_shared(empty0, 1);
+      uint32_t s = 0, ph = 0;
+      int g = 0;
+      bool ok = true;
+      for (int t = cluster; t < p.tiles && ok; t += clusters) {
+        const PairTile tl = pair_tile(p, t);
+        const PairProblem& q = p.prob[tl.pi];
+        const CUtensorMap* tm = tl.pi ? &tm_x1 : &tm_x0;
+        const int row0 = tl.mt * 256 + static_cast<int>(rank) * 128;
+        const uint8_t* wsrc = q.tiles + chunk_offset(tl.nt, 0, q.k_blocks) + rank * kHalfBytes;
+        const int kbs = q.k_blocks;
+        for (int kb = 0; kb < kbs; ++kb, ++g) {
+          if (g >= kPairStages) {
+            if (!mbar_wait_cl(empty0 + 8 * s, ph ^ 1, &abort_flag, status, kDevTimeoutTma)) {
+              ok = false;
+              break;
+            }
+            if (rank == 0) mbar_arrive_cluster(peer_empty0 + 8 * s);
+          }
+          uint8_t* st = smem + s * kPairStage;
+          mbar_arrive_expect_tx(&full[s], kPairABytes + kHalfBytes);
+          tma_load_2d(st, tm, &full[s], kb * kKB, row0);
+          bulk_load(st + kPairOffPk, wsrc + static_cast<size_t>(kb) * kChunkBytes, kHalfBytes, &full[s]);
+          if (++s == kPairStages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
       }
-      if (abort_flag) {
-        for (int kb = (issued > kGemmStages ? issued - kGemmStages : 0); kb < issued; ++kb) {
-          const uint32_t a = smem_u32(&full[kb % kGemmStages]);
+      if (!ok) {
+        // Let the copies already issued land before the CTA can exit.
+        for (int j = (g > kPairStages ? g - kPairStages : 0); j < g; ++j) {
+          const uint32_t a = smem_u32(&full[j % kPairStages]);
           const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(a, (kb / kGemmStages) & 1) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
+          while (!mbar_try_wait(a, (j / kPairStages) & 1) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- UMMA
-      bool ok = true;
+    if (lane == 0 && rank == 0) {
+      // ---------------------------------------------------------- UMMA (even CTA)
+      // Lean loop: the tensor core's queue of pending MMAs is short, so every
+      // cycle this thread spends outside the issue of MMAs can idle it.
       const uint32_t s0 = smem_u32(smem);
-      for (int kb = 0; kb < KB && ok; ++kb) {
-        const int s = kb % kGemmStages, use = kb / kGemmStages;
-        ok = mbar_wait(&full[s], use & 1, &abort_flag, status, kDevTimeoutMma) &&
-             mbar_wait(&bready[s], use & 1, &abort_flag, status, kDevTimeoutMma);
-        if (!ok) break;
+      const uint32_t bready0 = smem_u32(&bready[0]);
+      const uint32_t empty0 = smem_u32(&empty[0]);
+      const uint64_t da0 = sdesc_sw128(s0, 16, 1024);
+      const uint64_t db0 = sdesc_sw128(s0 + kPairOffB, 16, 1024);
+      uint32_t s = 0, ph = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = cluster; t < p.tiles && ok; t += clusters, ++i) {
+        const int kbs = p.prob[pair_tile(p, t).pi].k_blocks;
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait_cl(smem_u32(&acce[b]), ((i >> 1) + 1) & 1, &abort_flag, status, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t st = s0 + s * L::kStageBytes;
-        const uint64_t db = sdesc_sw128(st + L::kOffB, 16, 1024);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const uint64_t da = sdesc_sw128(st + L::kOffA + mt * 16384, 16, 1024);
+        const uint32_t d = tmem + b * 256;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!mbar_wait_cl(bready0 + 8 * s, ph, &abort_flag, status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t off = (s * kPairStage) >> 4;  // stage offset in the descriptors' 16-byte units
 #pragma unroll
           for (int kk = 0; kk < kKB / 16; ++kk)
-            umma_ss(tmem + mt * 256, da + (kk * 2), db + (kk * 2), kIdescGemm, (kb > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&empty[s]);
-      }
-      umma_commit(acc);  // arrives once every UMMA above has completed (also on abort)
-      mbar_wait(acc, 0, &abort_flag, status, kDevTimeoutMma);
-    }
-  } else if (warp >= kDequantWarp0) {
-    // ------------------------------------------------------------ dequant
-    const int dt = threadIdx.x - kDequantWarp0 * 32;  // 0..255
-    bool ok = true;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kGemmStages, use = kb / kGemmStages;
-      ok = mbar_wait_warp(&full[s], use & 1, &abort_flag, status, kDevTimeoutProducer);
-      if (!ok) break;
-      const uint8_t* pk = smem + s * L::kStageBytes + L::kOffPk;
-      uint8_t* bt = smem + s * L::kStageBytes + L::kOffB;
-      {
-        const int row = dt >> 1, hw = dt & 1;  // row of the B tile, half (words 4*hw .. 4*hw+3)
-        const uint4 w4 = *reinterpret_cast<const uint4*>(pk + row * 32 + hw * 16);
-        const float sc = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(pk + kOffScale)[row]);
-        const float bi = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(pk + kOffBias)[row]);
-        uint8_t* brow = bt + (row >> 3) * 1024 + (row & 7) * 128;
-        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = hw * 4 + i;
-          *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = dequant_word(ws[i], sc, bi);
-        }
-      }
-      fence_async_shared();  // generic-proxy stores -> visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bready[s]);
-    }
-    // ------------------------------------------------------------ epilogue
-    if (ok) ok = mbar_wait_warp(acc, 0, &abort_flag, status, kDevTimeoutEpilogue);
-    if (ok) {
-      tc_fence_after();
-      const int quad = warp & 3;
-      const int quarter = (warp - kDequantWarp0) >> 2;  // columns [64*quarter, +64)
-      const int n0 = nt * kTileN + quarter * 64;
-#pragma unroll 1
-      for (int mt = 0; mt < MT; ++mt) {
-        const int row = m0 + mt * 128 + quad * 32 + lane;
-        const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + mt * 256 + quarter * 64;
-#pragma unroll 1
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c0, r);
-          tmem_wait_ld();
-          const int col = n0 + c0;
-          if (row < p.m && col < p.n) {
-            if (p.mode == kOutResidualGate) {
-              // Gated residual (dd_gate_add, DirectDiTKernels.swift:208-221): y += gate * acc, f32.
-              float* yr = static_cast<float*>(p.y) + static_cast<int64_t>(row) * p.ldy + col;
-              if (p.vec && col + 32 <= p.n) {
-#pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                  const float4 g = __ldg(reinterpret_cast<const float4*>(p.gate + col + i));
-                  float4 v = *reinterpret_cast<float4*>(yr + i);
-                  v.x = fmaf(g.x, __uint_as_float(r[i]), v.x);
-                  v.y = fmaf(g.y, __uint_as_float(r[i + 1]), v.y);
-                  v.z = fmaf(g.z, __uint_as_float(r[i + 2]), v.z);
-                  v.w = fmaf(g.w, __uint_as_float(r[i + 3]), v.w);
-                  *reinterpret_cast<float4*>(yr + i) = v;
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col + i < p.n) yr[i] = fmaf(p.gate[col + i], __uint_as_float(r[i]), yr[i]);
-              }
-            } else if (p.mode == kOutF32) {
-              float* yr = static_cast<float*>(p.y) + static_cast<int64_t>(row) * p.ldy + col;
-              if (p.vec && col + 32 <= p.n) {
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                  *reinterpret_cast<float4*>(yr + i) = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
-                                                                   __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col + i < p.n) yr[i] = __uint_as_float(r[i]);
-              }
-            } else {
-              uint16_t* yr = static_cast<uint16_t*>(p.y) + static_cast<int64_t>(row) * p.ldy + col;
-              uint32_t pk[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-              if (p.vec && col + 32 <= p.n) {
-#pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                  *reinterpret_cast<uint4*>(yr + 2 * i) = make_uint4(pk[i], pk[i + 1], pk[i + 2], pk[i + 3]);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col + i < p.n) yr[i] = static_cast<uint16_t>((i & 1) ? (pk[i >> 1] >> 16) : (pk[i >> 1] & 0xFFFFu));
-              }
-            }
+            umma_ss_pair(d, da0 + off + kk * 2, db0 + off + kk * 2, kIdescPair, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(empty0 + 8 * s);
+          if (++s == kPairStages) {
+            s = 0;
+            ph ^= 1;
           }
         }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&accf[b]));
+        umma_commit_pair(mapa_shared(smem_u32(&accf[b]), 1));
+      }
+      // Arrives once every MMA above has completed; waited for also on abort
+      // (hence a flag of its own), so no MMA is in flight at the teardown.
+      umma_commit_pair(smem_u32(drain));
+      int no_abort = 0;
+      mbar_wait_cl(smem_u32(drain), 0, &no_abort, status, kDevTimeoutMma);
+    }
+  } else if (warp >= kPairEpi0 && warp < kPairEpi0 + 4) {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    int i = 0;
+    for (int t = cluster; t < p.tiles; t += clusters, ++i) {
+      const PairTile tl = pair_tile(p, t);
+      const PairProblem& q = p.prob[tl.pi];
+      const int b = i & 1;
+      if (!mbar_wait_warp_cl(smem_u32(&accf[b]), (i >> 1) & 1, &abort_flag, status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = tl.mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 256;
+#pragma unroll 1
+      for (int c0 = 0; c0 < 256; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c0, r);
+        tmem_wait_ld();
+        const int col = tl.nt * kTileN + c0;
+        if (row < q.m && col < q.n) store_run(q, row, col, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[b]), 0));
+    }
+  } else if (warp >= kPairDeq0) {
+    // ------------------------------------------------------------ dequant
+    const int dw = warp - kPairDeq0;
+    const int group = dw / kPairDeqWarps;
+    const int dt = (dw % kPairDeqWarps) * 32 + lane;  // 0 .. 128 * kPairSplit - 1
+    const int row = dt / kPairSplit, part = dt % kPairSplit;  // row of this CTA's B half; words part*kPairWords ..
+    uint8_t* bdst = smem + kPairOffB + row * 128;
+    const uint32_t full0 = smem_u32(&full[0]);
+    const uint32_t bready_lead0 = mapa_shared(smem_u32(&bready[0]), 0);
+    uint32_t s = 0, ph = 0;
+    int g = 0;
+    bool ok = true;
+    for (int t = cluster; t < p.tiles && ok; t += clusters) {
+      const int kbs = p.prob[pair_tile(p, t).pi].k_blocks;
+      for (int kb = 0; kb < kbs; ++kb, ++g) {
+        const uint32_t cs = s, cph = ph;  // this K block's stage and phase
+        if (++s == kPairStages) {
+          s = 0;
+          ph ^= 1;
+        }
+        if (kPairGroups > 1 && g % kPairGroups != group) continue;
+        if (!mbar_wait_warp_cl(full0 + 8 * cs, cph, &abort_flag, status, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* pk = smem + cs * kPairStage + kPairOffPk;
+        uint32_t ws[kPairWords];
+        if (kPairWords >= 4) {
+#pragma unroll
+          for (int j = 0; j < kPairWords; j += 4) {
+            const uint4 w4 = *reinterpret_cast<const uint4*>(pk + row * 32 + part * kPairWords * 4 + j * 4);
+            ws[j] = w4.x;
+            ws[j + 1] = w4.y;
+            ws[j + 2] = w4.z;
+            ws[j + 3] = w4.w;
+          }
+        } else {
+          const uint2 w2 = *reinterpret_cast<const uint2*>(pk + row * 32 + part * 8);
+          ws[0] = w2.x;
+          ws[kPairWords - 1] = w2.y;
+        }
+        const uint32_t s16 = *reinterpret_cast<const uint16_t*>(pk + 4096 + row * 2);
+        const uint32_t b16 = *reinterpret_cast<const uint16_t*>(pk + 4352 + row * 2);
+        uint8_t* brow = bdst + cs * kPairStage;
+        if (one_rounding_exact(s16, b16)) {
+          const uint32_t s2 = s16 | (s16 << 16), b2 = b16 | (b16 << 16);
+#pragma unroll
+          for (int j = 0; j < kPairWords; ++j) {
+            const int c = part * kPairWords + j;
+            *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = dequant_word_fast(ws[j], s2, b2);
+          }
+        } else {
+          const float sc = __uint_as_float(s16 << 16), bi = __uint_as_float(b16 << 16);
+#pragma unroll
+          for (int j = 0; j < kPairWords; ++j) {
+            const int c = part * kPairWords + j;
+            *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = dequant_word_exact(ws[j], sc, bi);
+          }
+        }
+        fence_async_shared();  // generic-proxy stores -> visible to the pair's tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(bready_lead0 + 8 * cs);
       }
     }
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // no peer access to this CTA's shared or tensor memory after this point
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, MT * 256);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -387,10 +603,10 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   for (int g = 0; g < kGemvMaxKbps; ++g) {
     if (active && g < nkb) {
       const uint8_t* chunk = p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks);
-      wv[2 * g] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32));
-      wv[2 * g + 1] = __ldg(reinterpret_cast<const uint4*>(chunk + r * 32) + 1);
-      sv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffScale) + r);
-      bv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + kOffBias) + r);
+      wv[2 * g] = __ldg(reinterpret_cast<const uint4*>(chunk + pk_off(r)));
+      wv[2 * g + 1] = __ldg(reinterpret_cast<const uint4*>(chunk + pk_off(r)) + 1);
+      sv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + sc_off(r)));
+      bv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + bi_off(r)));
     }
   }
   // 2. Stage this split's x slice as f32, then per-group sums (one warp per
@@ -430,12 +646,11 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
       for (int mr = 0; mr < R; ++mr) tq[mr] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint32_t lo = ws[c] & 0x0F0F0F0Fu, hi = (ws[c] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float ql = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + i));
-          const float qh = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + i));
-          const float2 q = fadd2(make_float2(ql, qh), make_float2(-8388608.0f, -8388608.0f));
+          const uint32_t t = code_pair_128(ws[c], i);  // codes 2i, 2i+1 of the (permuted) word
+          const float2 q = fadd2(make_float2(__uint_as_float(t << 16), __uint_as_float(t & 0xFFFF0000u)),
+                                 make_float2(-128.0f, -128.0f));
           const int kk = g * kKB + c * 8 + 2 * i;  // codes kk, kk+1
 #pragma unroll
           for (int mr = 0; mr < R; ++mr)
@@ -486,30 +701,6 @@ int validate_q(aex_ctx* ctx, const void* packed, const void* scales, const void*
   return AEX_OK;
 }
 
-template <int MT>
-int launch_gemm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
-                int mode, const float* gate, cudaStream_t s) {
-  using L = qmm::GemmLayout<MT>;
-  CUtensorMap tx;
-  uint64_t dims[2] = {static_cast<uint64_t>(w->k), static_cast<uint64_t>(m)};
-  uint64_t strides[1] = {static_cast<uint64_t>(ldx) * 2};
-  uint32_t box[2] = {64, 128};
-  if (int r = make_tmap(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, 2, dims, strides, box,
-                        CU_TENSOR_MAP_SWIZZLE_128B))
-    return r;
-  const int esz = mode == qmm::kOutBf16 ? 2 : 4;
-  const int vec = ((reinterpret_cast<uintptr_t>(y) & 15) == 0 && (ldy * esz) % 16 == 0 &&
-                   (reinterpret_cast<uintptr_t>(gate) & 15) == 0)
-                      ? 1
-                      : 0;
-  qmm::GemmParams p{w->tiles, m, w->n, w->k_blocks, y, ldy, mode, gate, vec};
-  auto kern = qmm::gemm_kernel<MT>;
-  AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem));
-  dim3 grid(w->n_tiles, (m + 128 * MT - 1) / (128 * MT));
-  kern<<<grid, qmm::kGemmThreads, L::kSmem, s>>>(tx, p, ctx->d_status);
-  return check_launch(ctx, "qmm gemm_kernel");
-}
-
 template <int R>
 int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
                 int mode, const float* gate, cudaStream_t s) {
@@ -549,22 +740,112 @@ int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
 
 }  // namespace
 
+namespace {
+
+int pair_vec(const QmmJob& j) {
+  const int esz = j.mode == qmm::kOutBf16 ? 2 : 4;
+  return ((reinterpret_cast<uintptr_t>(j.y) & 15) == 0 && (j.ldy * esz) % 16 == 0 &&
+          (reinterpret_cast<uintptr_t>(j.gate) & 15) == 0)
+             ? 1
+             : 0;
+}
+
+// The CTA-pair GEMM over one or two jobs (each m > 16).
+int launch_gemm_pair(aex_ctx* ctx, const QmmJob* jobs, int n_jobs, cudaStream_t s) {
+  CUtensorMap tm[qmm::kPairMaxProblems];
+  qmm::PairParams p{};
+  p.n_prob = n_jobs;
+  int tiles = 0;
+  for (int i = 0; i < n_jobs; ++i) {
+    const QmmJob& j = jobs[i];
+    uint64_t dims[2] = {static_cast<uint64_t>(j.w->k), static_cast<uint64_t>(j.m)};
+    uint64_t strides[1] = {static_cast<uint64_t>(j.ldx) * 2};
+    uint32_t box[2] = {64, 128};
+    if (int r = make_tmap(ctx, &tm[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, j.x, 2, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+    qmm::PairProblem& q = p.prob[i];
+    q.tiles = j.w->tiles;
+    q.m = j.m;
+    q.n = j.w->n;
+    q.k_blocks = j.w->k_blocks;
+    q.m_tiles = (j.m + 255) / 256;
+    q.tile0 = tiles;
+    q.y = j.y;
+    q.ldy = j.ldy;
+    q.mode = j.mode;
+    q.gate = j.gate;
+    q.vec = pair_vec(j);
+    tiles += q.m_tiles * j.w->n_tiles;
+  }
+  if (n_jobs == 1) tm[1] = tm[0];
+  p.tiles = tiles;
+  auto kern = qmm::gemm_pair_kernel;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(qmm::kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = qmm::kPairSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, qmm::kPairSmem));
+  if (ctx->pair_clusters <= 0) {
+    // How many 2-CTA clusters of this kernel fit on the device at once (the
+    // persistent grid); at most one per SM pair.
+    cfg.gridDim = dim3(2 * (ctx->sm_count / 2), 1, 1);
+    int n = 0;
+    AEX_CUDA_TRY(ctx, cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    if (n <= 0) return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm: the CTA-pair GEMM cannot be resident on this device");
+    ctx->pair_clusters = n;
+  }
+  const int clusters = std::min(tiles, ctx->pair_clusters);
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  AEX_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], p, ctx->d_status));
+  return check_launch(ctx, "qmm gemm_pair_kernel");
+}
+
+bool gemv_path(const aex_qweight* w, int m) { return m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps; }
+
+int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
+  const aex_qweight* w = j.w;
+  if (gemv_path(w, j.m)) {
+    if (j.m <= 1) return launch_gemv<1>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
+    if (j.m <= 2) return launch_gemv<2>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
+    if (j.m <= 4) return launch_gemv<4>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
+    if (j.m <= 8) return launch_gemv<8>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
+    return launch_gemv<16>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
+  }
+  return launch_gemm_pair(ctx, &j, 1, s);
+}
+
+int check_job(aex_ctx* ctx, const QmmJob& j) {
+  if (j.m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
+  if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
+  return AEX_OK;
+}
+
+}  // namespace
+
 int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy, int mode,
             const float* gate, cudaStream_t s) {
-  if (m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
-  if (mode == qmm::kOutResidualGate && !gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
-  if (m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps) {
-    if (m <= 1) return launch_gemv<1>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
-    if (m <= 2) return launch_gemv<2>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
-    if (m <= 4) return launch_gemv<4>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
-    if (m <= 8) return launch_gemv<8>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
-    return launch_gemv<16>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+  const QmmJob j{w, x, ldx, m, y, ldy, mode, gate};
+  if (int r = check_job(ctx, j)) return r;
+  return run_one(ctx, j, s);
+}
+
+int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s) {
+  if (int r = check_job(ctx, a)) return r;
+  if (int r = check_job(ctx, b)) return r;
+  if (!gemv_path(a.w, a.m) && !gemv_path(b.w, b.m)) {
+    const QmmJob jobs[2] = {a, b};
+    return launch_gemm_pair(ctx, jobs, 2, s);
   }
-#ifndef AEX_QMM_MT2_MIN_M
-#define AEX_QMM_MT2_MIN_M 2048
-#endif
-  if (m >= AEX_QMM_MT2_MIN_M) return launch_gemm<2>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
-  return launch_gemm<1>(ctx, w, x, ldx, m, y, ldy, mode, gate, s);
+  if (int r = run_one(ctx, a, s)) return r;
+  return run_one(ctx, b, s);
 }
 
 }  // namespace aex

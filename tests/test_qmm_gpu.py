@@ -127,3 +127,43 @@ def test_qmm_strided_io_and_errors(cuda_ctx):
     with pytest.raises(_lib.AexError):
         w(torch.zeros(4, k + 8, dtype=torch.bfloat16, device="cuda")[:, 4:4 + k])  # 8-byte misaligned rows
     assert cuda_ctx.device_status() == 0
+
+
+def test_gemm_weights_bit_exact_identity(cuda_ctx):
+    """x = identity: the GEMM's f32 output is then exactly the bf16 weights it
+    dequantized in registers, which must equal the reference dequant bit for bit
+    on both of its paths (one bf16 rounding where the bound allows it, the f32
+    path elsewhere): random groups, the golden double-rounding cases, wide
+    scale/bias exponent gaps, zeros and subnormal scales."""
+    n, k = 256, 256
+    rng = np.random.default_rng(11)
+    tp, ts, tb = qmm.synthetic_weight(n, k, seed=5)
+    packed, scales, biases = _np_u32(tp).copy(), _np_u16(ts).copy(), _np_u16(tb).copy()
+    with open(os.path.join(GOLD, "bf16_dequant.json")) as f:
+        g = json.load(f)
+    cases = [(c["q"] * 0x11111111, c["scale"], c["bias"]) for c in g["double_rounding"]]
+    cases += [(w["packed"], w["scale"], w["bias"]) for w in g["dequant_words"]]
+    r = 0
+    for word, sc, bi in cases:  # rows 0.. : one golden case per (row, group 0)
+        packed[r, :8] = word
+        scales[r, 0], biases[r, 0] = sc, bi
+        r += 1
+    gaps = [(0x3F80, 0x3F80 - (20 << 7)), (0x3F80 - (20 << 7), 0x3F80), (0x0003, 0x3C00), (0x0000, 0x3D00),
+            (0x3D00, 0x0000), (0x4700, 0xB900), (0xB900, 0x4700)]
+    for sc, bi in gaps:  # further rows: wide gaps / zeros / subnormals in group 1
+        packed[r, 8:16] = rng.integers(0, 2**32, 8, dtype=np.uint64).astype(np.uint32)
+        scales[r, 1], biases[r, 1] = sc, bi
+        r += 1
+    assert r < n
+    ref = O.dequant_q4(packed, scales, biases, n, k)  # [n, k] bf16 bits
+    tp = torch.from_numpy(packed.view(np.int32)).cuda()
+    ts = torch.from_numpy(scales.view(np.int16)).view(torch.bfloat16).cuda()
+    tb = torch.from_numpy(biases.view(np.int16)).view(torch.bfloat16).cuda()
+    w = qmm.QuantizedWeight(tp, ts, tb)
+    eye = torch.eye(k, dtype=torch.bfloat16, device="cuda")
+    y = w(eye, out_dtype=torch.float32)  # y[m, n] = W[n, m]
+    torch.cuda.synchronize()
+    got = O.f32_to_bf16(y.cpu().numpy().T.copy())
+    # A zero weight sums to +0 in the accumulator whatever its sign.
+    ref = np.where(ref == 0x8000, np.uint16(0), ref)
+    assert np.array_equal(got, ref), np.argwhere(got != ref)[:8]
