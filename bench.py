@@ -293,7 +293,7 @@ def measure_qmm(ctx, dev, iters=20):
             nbytes = wbytes + 2 * M * K + 2 * M * N
             out[f"M{M}_N{N}"] = {"ms": ms, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
                                  "gbs": nbytes / (ms * 1e-3) / 1e9,
-                                 "kernel": "gemv_kernel" if M <= 16 else "gemm_kernel",
+                                 "kernel": "gemv_kernel" if M <= 16 else "gemm_pair_kernel",
                                  "bound": "hbm" if M <= 16 else "tensor"}
         del ws
     return out
