@@ -112,6 +112,20 @@ int fuse3(aex_dit* d, const std::string& a, const std::string& b, const std::str
   return AEX_OK;
 }
 
+// "<name>#glu": the gate/up-interleaved copy of a linear whose last 2 * mlp
+// rows are [gate | up] (qmm_glu_interleave), built once and dropped when
+// <name> is re-loaded.
+int glu_copy(aex_dit* d, const std::string& name, int plain_rows, cudaStream_t s) {
+  const std::string out = name + "#glu";
+  if (d->lin.count(out)) return AEX_OK;
+  auto it = d->lin.find(name);
+  if (it == d->lin.end()) return set_error(d->ctx, AEX_ERR_INVALID_ARG, "missing linear %s", name.c_str());
+  aex_qweight* w = nullptr;
+  if (int r = qmm_glu_interleave(d->ctx, it->second, plain_rows, d->mlp, &w, s)) return r;
+  d->lin[out] = w;
+  return AEX_OK;
+}
+
 const aex_qweight* need_lin(aex_dit* d, const std::string& name, int n, int k) {
   auto it = d->lin.find(name);
   if (it == d->lin.end()) {
@@ -175,9 +189,9 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   AEX_NEED(qkv_t, need_lin(d, blk("transformer_blocks", i, "attn.add_qkv"), 3 * C, C));
   AEX_NEED(out_i, need_lin(d, blk("transformer_blocks", i, "attn.to_out"), C, C));
   AEX_NEED(out_t, need_lin(d, blk("transformer_blocks", i, "attn.to_add_out"), C, C));
-  AEX_NEED(ffi_i, need_lin(d, blk("transformer_blocks", i, "ff.linear_in"), 2 * mlp, C));
+  AEX_NEED(ffi_i, need_lin(d, blk("transformer_blocks", i, "ff.linear_in#glu"), 2 * mlp, C));
   AEX_NEED(ffo_i, need_lin(d, blk("transformer_blocks", i, "ff.linear_out"), C, mlp));
-  AEX_NEED(ffi_t, need_lin(d, blk("transformer_blocks", i, "ff_context.linear_in"), 2 * mlp, C));
+  AEX_NEED(ffi_t, need_lin(d, blk("transformer_blocks", i, "ff_context.linear_in#glu"), 2 * mlp, C));
   AEX_NEED(ffo_t, need_lin(d, blk("transformer_blocks", i, "ff_context.linear_out"), C, mlp));
   AEX_NEED(nq, need_norm(d, blk("transformer_blocks", i, "attn.norm_q")));
   AEX_NEED(nk, need_norm(d, blk("transformer_blocks", i, "attn.norm_k")));
@@ -199,14 +213,16 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   // MLP half (per stream)
   AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + 4 * C, mt + 3 * C, eps_ln, NHt, C, s));
   AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + 4 * C, mi + 3 * C, eps_ln, NHi, C, s));
-  const int64_t pf = 2 * mlp;
   uint16_t* SWt = d->ATT;                                   // [lt, mlp]
   uint16_t* SWi = d->ATT + static_cast<int64_t>(lt) * mlp;  // [li, mlp]
-  uint16_t* Pi = d->PROJ + static_cast<int64_t>(lt) * pf;
-  AEX_TRY(qmm_run2(d->ctx, QmmJob{ffi_t, NHt, C, lt, d->PROJ, pf, 0, nullptr},
-                   QmmJob{ffi_i, NHi, C, li, Pi, pf, 0, nullptr}, s));
-  // Text rows then image rows are contiguous in PROJ and in SW: one SwiGLU over all J rows.
-  AEX_TRY(glue::swiglu(d->ctx, d->PROJ, d->PROJ + mlp, pf, J, mlp, SWt, mlp, s));
+  // linear_in with the SwiGLU in its epilogue (gate/up interleaved weights): silu(g) * u straight into SW.
+  QmmJob ff_t{ffi_t, NHt, C, lt, nullptr, 0, 0, nullptr};
+  QmmJob ff_i{ffi_i, NHi, C, li, nullptr, 0, 0, nullptr};
+  ff_t.glu_tile0 = ff_i.glu_tile0 = 0;
+  ff_t.y2 = SWt;
+  ff_i.y2 = SWi;
+  ff_t.ldy2 = ff_i.ldy2 = mlp;
+  AEX_TRY(qmm_run2(d->ctx, ff_t, ff_i, s));
   AEX_TRY(qmm_run2(d->ctx, QmmJob{ffo_t, SWt, mlp, lt, Xt, C, 2, mt + 5 * C},
                    QmmJob{ffo_i, SWi, mlp, li, Xi, C, 2, mi + 5 * C}, s));
   return AEX_OK;
@@ -214,19 +230,23 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
 
 int single_block(aex_dit* d, int i, cudaStream_t s) {
   const int C = d->C, J = d->J, mlp = d->mlp;
-  AEX_NEED(proj, need_lin(d, blk("single_transformer_blocks", i, "attn.to_qkv_mlp_proj"), d->proj, C));
+  AEX_NEED(proj, need_lin(d, blk("single_transformer_blocks", i, "attn.to_qkv_mlp_proj#glu"), d->proj, C));
   AEX_NEED(out, need_lin(d, blk("single_transformer_blocks", i, "attn.to_out"), C, d->cat));
   AEX_NEED(nq, need_norm(d, blk("single_transformer_blocks", i, "attn.norm_q")));
   AEX_NEED(nk, need_norm(d, blk("single_transformer_blocks", i, "attn.norm_k")));
   const float* ms = d->MOD_SINGLE;
   AEX_TRY(glue::ln_mod(d->ctx, d->X, C, J, C, ms + C, ms, d->cfg.ln_eps, d->NH, C, s));
   const int64_t pp = d->proj;
-  AEX_TRY(qmm_run(d->ctx, proj, d->NH, C, J, d->PROJ, pp, 0, nullptr, s));
+  // Q|K|V columns into PROJ; the gate/up tiles (interleaved) go through the SwiGLU epilogue into
+  // columns [C, C + mlp) of the concat buffer (ParallelSelfAttention.swift:117-123).
+  QmmJob pj{proj, d->NH, C, J, d->PROJ, pp, 0, nullptr};
+  pj.glu_tile0 = 3 * C / 256;
+  pj.y2 = d->ATT + C;
+  pj.ldy2 = d->cat;
+  AEX_TRY(qmm_run_job(d->ctx, pj, s));
   const int64_t qs[3] = {static_cast<int64_t>(J) * pp, pp, 128};
   AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, d->H, nq, nk, nullptr, nullptr, 0,
                          d->cfg.rms_eps, d->COS, d->SIN, d->PREP, s));
-  // SwiGLU(g, u) into columns [C, C + mlp) of the concat buffer (ParallelSelfAttention.swift:117-123)
-  AEX_TRY(glue::swiglu(d->ctx, d->PROJ + 3 * C, d->PROJ + 3 * C + mlp, pp, J, mlp, d->ATT + C, d->cat, s));
   AEX_TRY(attend(d, d->PROJ + 2 * C, pp, d->ATT, d->cat, s));
   AEX_TRY(qmm_run(d->ctx, out, d->ATT, d->cat, J, d->X, C, 2, ms + 2 * C, s));
   return AEX_OK;
@@ -238,8 +258,11 @@ int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s) {
   const int C = d->C, lt = d->cfg.l_txt, li = d->cfg.l_img, ic = d->cfg.in_channels;
   AEX_NEED(xemb, need_lin(d, "x_embedder", C, ic));
   AEX_NEED(pout, need_lin(d, "proj_out", ic, C));
-  // Fuse the per-stream Q|K|V linears of the double blocks once.
+  // Fuse the per-stream Q|K|V linears of the double blocks and interleave the gate/up halves of the
+  // feed-forward inputs once.
   for (int i = 0; i < d->cfg.n_double; ++i) {
+    AEX_TRY(glu_copy(d, blk("transformer_blocks", i, "ff.linear_in"), 0, s));
+    AEX_TRY(glu_copy(d, blk("transformer_blocks", i, "ff_context.linear_in"), 0, s));
     if (!d->lin.count(blk("transformer_blocks", i, "attn.qkv")))
       AEX_TRY(fuse3(d, blk("transformer_blocks", i, "attn.to_q"), blk("transformer_blocks", i, "attn.to_k"),
                     blk("transformer_blocks", i, "attn.to_v"), blk("transformer_blocks", i, "attn.qkv"), s));
@@ -247,6 +270,8 @@ int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s) {
       AEX_TRY(fuse3(d, blk("transformer_blocks", i, "attn.add_q_proj"), blk("transformer_blocks", i, "attn.add_k_proj"),
                     blk("transformer_blocks", i, "attn.add_v_proj"), blk("transformer_blocks", i, "attn.add_qkv"), s));
   }
+  for (int i = 0; i < d->cfg.n_single; ++i)
+    AEX_TRY(glu_copy(d, blk("single_transformer_blocks", i, "attn.to_qkv_mlp_proj"), 3 * d->C, s));
   // Embedders: image rows from x_embedder (f32 out), text rows from the projected context.
   AEX_TRY(glue::f32_to_bf16(d->ctx, latents, static_cast<int64_t>(li) * ic, d->LAT16, s));
   AEX_TRY(qmm_run(d->ctx, xemb, d->LAT16, ic, li, d->X + static_cast<int64_t>(lt) * C, C, 1, nullptr, s));
@@ -356,8 +381,13 @@ int aex_dit_load_linear(aex_dit* d, const char* name, const uint32_t* packed, co
   auto it = d->lin.find(name);
   if (it != d->lin.end()) aex_qweight_destroy(it->second);
   d->lin[name] = w;
-  // A re-loaded part invalidates a fused Q|K|V built from it.
+  // A re-loaded part invalidates a fused Q|K|V or a gate/up-interleaved copy built from it.
   const std::string s(name);
+  auto glu = d->lin.find(s + "#glu");
+  if (glu != d->lin.end()) {
+    aex_qweight_destroy(glu->second);
+    d->lin.erase(glu);
+  }
   for (const char* part : {"attn.to_q", "attn.to_k", "attn.to_v", "attn.add_q_proj", "attn.add_k_proj",
                            "attn.add_v_proj"}) {
     const std::string p(part);

@@ -6,7 +6,8 @@
 //   ln_mod      LayerNorm (no affine, eps) + AdaLN modulate (1+scale)*n + shift -> bf16
 //               (dd_ln_mod_prescale :15-57; Flux2TransformerBlock norm1/modApply,
 //               Sources/ImarelloDiT/TransformerBlock.swift:42-44, ModulationOps.swift)
-//   swiglu      silu(g) * u -> bf16 (dd_swiglu_pitched :138-159; FeedForward.swift:11-24)
+//   (SwiGLU, dd_swiglu_pitched :138-159, is fused into the feed-forward GEMM's
+//   epilogue: qmm_sm100.cu, swiglu1)
 //   gate_add    x += gate * v, x f32 (dd_gate_add :208-221) — used where the
 //               producing GEMM did not already fuse it
 //   euler       lat_out = lat_in + dt * v (Flux2Scheduler.step, Flux2Scheduler.swift:101-109)
@@ -74,26 +75,6 @@ __global__ void __launch_bounds__(kRowThreads) ln_mod_kernel(const float* __rest
   }
 }
 
-// silu(g) * u over [rows, width] with pitched inputs; 8 columns per thread.
-__global__ void swiglu_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, int64_t ld_in,
-                              int rows, int width, uint16_t* __restrict__ out, int64_t ld_out) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int per_row = width / 8;
-  if (idx >= static_cast<int64_t>(rows) * per_row) return;
-  const int64_t r = idx / per_row;
-  const int c = static_cast<int>(idx % per_row) * 8;
-  const uint4 gv = *reinterpret_cast<const uint4*>(g + r * ld_in + c);
-  const uint4 uv = *reinterpret_cast<const uint4*>(u + r * ld_in + c);
-  const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float g0 = bf16lo_to_f32(ga[i]), g1 = bf16hi_to_f32(ga[i]);
-    const float u0 = bf16lo_to_f32(ua[i]), u1 = bf16hi_to_f32(ua[i]);
-    o[i] = pack_bf16x2(g0 / (1.f + __expf(-g0)) * u0, g1 / (1.f + __expf(-g1)) * u1);
-  }
-  *reinterpret_cast<uint4*>(out + r * ld_out + c) = make_uint4(o[0], o[1], o[2], o[3]);
-}
 
 __global__ void gate_add_kernel(float* __restrict__ x, int64_t ldx, int rows, int C, const float* __restrict__ gate,
                                 const uint16_t* __restrict__ v, int64_t ldv, float scale) {
@@ -156,15 +137,6 @@ int ln_mod(aex_ctx* ctx, const float* x, int64_t ldx, int rows, int C, const flo
   return check_launch(ctx, "ln_mod_kernel");
 }
 
-int swiglu(aex_ctx* ctx, const void* g, const void* u, int64_t ld_in, int rows, int width, void* out, int64_t ld_out,
-           cudaStream_t s) {
-  if (rows <= 0) return AEX_OK;
-  if (width % 8 || ld_in % 8 || ld_out % 8) return set_error(ctx, AEX_ERR_INVALID_ARG, "swiglu: widths must be multiples of 8");
-  const int64_t n = static_cast<int64_t>(rows) * (width / 8);
-  swiglu_kernel<<<blocks_for(n, 256), 256, 0, s>>>(static_cast<const uint16_t*>(g), static_cast<const uint16_t*>(u),
-                                                    ld_in, rows, width, static_cast<uint16_t*>(out), ld_out);
-  return check_launch(ctx, "swiglu_kernel");
-}
 
 int gate_add(aex_ctx* ctx, float* x, int64_t ldx, int rows, int C, const float* gate, const void* v, int64_t ldv,
              float scale, cudaStream_t s) {

@@ -10,8 +10,6 @@ namespace glue {
 int ln_mod(aex_ctx* ctx, const float* x, int64_t ldx, int rows, int C, const float* scale, const float* shift,
            float eps, void* y, int64_t ldy, cudaStream_t s);
 // out_bf16[r, c] = silu(g[r, c]) * u[r, c], c < width.
-int swiglu(aex_ctx* ctx, const void* g, const void* u, int64_t ld_in, int rows, int width, void* out, int64_t ld_out,
-           cudaStream_t s);
 // x_f32[r, c] += gate[c] * scale * v_bf16[r, c] (gate NULL: 1).
 int gate_add(aex_ctx* ctx, float* x, int64_t ldx, int rows, int C, const float* gate, const void* v, int64_t ldv,
              float scale, cudaStream_t s);

@@ -74,8 +74,20 @@ struct QmmJob {
   int64_t ldy;
   int mode;
   const float* gate;
+  // Weight tiles from glu_tile0 on are gate/up interleaved (qmm_glu_interleave):
+  // their output is silu(g) * u, bf16, into y2 (row pitch ldy2) at column
+  // (tile - glu_tile0) * 128.
+  int glu_tile0 = 1 << 30;
+  uint16_t* y2 = nullptr;
+  int64_t ldy2 = 0;
 };
+int qmm_run_job(aex_ctx* ctx, const QmmJob& j, cudaStream_t s);
 int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s);
+// A copy of `src` (n = plain_rows + 2 * mlp rows: plain rows, then gate rows,
+// then up rows) whose tiles after the plain ones each hold 128 gate rows then
+// the matching 128 up rows, for the SwiGLU epilogue.
+int qmm_glu_interleave(aex_ctx* ctx, const aex_qweight* src, int plain_rows, int mlp, aex_qweight** out,
+                       cudaStream_t s);
 // QK-RMSNorm + RoPE pre-pass into head-major scratch [2][B][H][S][128]; tokens
 // s < split use (wq_a, wk_a), the others (wq, wk).
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,

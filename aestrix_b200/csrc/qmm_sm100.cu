@@ -173,6 +173,24 @@ __global__ void __launch_bounds__(256) dequant_tiles_kernel(const uint8_t* __res
   *reinterpret_cast<uint4*>(out + wi * 8) = dequant_word_exact(w, s, b);
 }
 
+// Copies 128-row chunk halves: dst half (t, kb, h) <- src half given by the
+// row maps below (qmm_glu_interleave); one CTA per destination half.
+__global__ void __launch_bounds__(256) glu_interleave_kernel(const uint8_t* __restrict__ src, int k_blocks,
+                                                             int plain_tiles, int mlp, uint8_t* __restrict__ dst) {
+  const int kb = blockIdx.x, h = blockIdx.y & 1, t = blockIdx.y >> 1;
+  int src_row;  // first of the 128 source rows of this destination half
+  if (t < plain_tiles) {
+    src_row = t * kTileN + h * 128;
+  } else {
+    const int j = t - plain_tiles;  // gate rows [128j, +128) then up rows, after the plain rows
+    src_row = plain_tiles * kTileN + h * mlp + j * 128;
+  }
+  const uint4* sp = reinterpret_cast<const uint4*>(src + chunk_offset(src_row / kTileN, kb, k_blocks) +
+                                                   ((src_row / 128) & 1) * kHalfBytes);
+  uint4* dp = reinterpret_cast<uint4*>(dst + chunk_offset(t, kb, k_blocks) + h * kHalfBytes);
+  for (int i = threadIdx.x; i < kHalfBytes / 16; i += blockDim.x) dp[i] = sp[i];
+}
+
 __global__ void __launch_bounds__(256) dequant_mlx_kernel(const uint32_t* __restrict__ packed,
                                                           const uint16_t* __restrict__ scales,
                                                           const uint16_t* __restrict__ biases, int n, int k_blocks,
@@ -188,6 +206,15 @@ __global__ void __launch_bounds__(256) dequant_mlx_kernel(const uint32_t* __rest
 
 // Epilogue modes of the GEMM and GEMV kernels.
 enum OutMode : int { kOutBf16 = 0, kOutF32 = 1, kOutResidualGate = 2 };
+
+// SwiGLU of one pair of bf16-rounded linear outputs (the storage points of
+// the reference's linear_in -> silu(g) * u, FeedForward.swift:11-24 and
+// dd_swiglu_pitched, DirectDiTKernels.swift:138-159).
+__device__ __forceinline__ float swiglu1(float g, float u) {
+  g = __uint_as_float(pack_bf16x2(g, 0.f) << 16);
+  u = __uint_as_float(pack_bf16x2(u, 0.f) << 16);
+  return g / (1.f + __expf(-g)) * u;
+}
 
 // ------------------------------------------------------------------ K2 CTA-pair GEMM
 // Two CTAs of a cluster compute one 256 x 256 output tile with
@@ -256,6 +283,12 @@ struct PairProblem {
   int mode;
   const float* gate;
   int vec;
+  // Weight tiles nt >= glu_tile0 hold 128 gate rows then 128 up rows (see
+  // qmm_glu_interleave); their epilogue writes silu(g) * u, bf16, into
+  // y2[row, (nt - glu_tile0) * 128 + c] (row pitch ldy2, 16-byte aligned).
+  int glu_tile0;
+  uint16_t* y2;
+  int64_t ldy2;
 };
 
 struct PairParams {
@@ -478,13 +511,35 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tc_fence_after();
       const int row = tl.mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 256;
+      if (tl.nt >= q.glu_tile0) {
+        // Gate columns [0, 128), up columns [128, 256) of this tile.
+        uint16_t* yr = q.y2 + static_cast<int64_t>(row) * q.ldy2 + (tl.nt - q.glu_tile0) * 128;
 #pragma unroll 1
-      for (int c0 = 0; c0 < 256; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c0, r);
-        tmem_wait_ld();
-        const int col = tl.nt * kTileN + c0;
-        if (row < q.m && col < q.n) store_run(q, row, col, r);
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t gr[32], ur[32];
+          tmem_ld32(tbase + c0, gr);
+          tmem_ld32(tbase + 128 + c0, ur);
+          tmem_wait_ld();
+          if (row < q.m) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack_bf16x2(swiglu1(__uint_as_float(gr[2 * i]), __uint_as_float(ur[2 * i])),
+                                  swiglu1(__uint_as_float(gr[2 * i + 1]), __uint_as_float(ur[2 * i + 1])));
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<uint4*>(yr + c0 + 2 * i) = make_uint4(pk[i], pk[i + 1], pk[i + 2], pk[i + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c0, r);
+          tmem_wait_ld();
+          const int col = tl.nt * kTileN + c0;
+          if (row < q.m && col < q.n) store_run(q, row, col, r);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -776,6 +831,9 @@ int launch_gemm_pair(aex_ctx* ctx, const QmmJob* jobs, int n_jobs, cudaStream_t 
     q.mode = j.mode;
     q.gate = j.gate;
     q.vec = pair_vec(j);
+    q.glu_tile0 = j.glu_tile0;
+    q.y2 = j.y2;
+    q.ldy2 = j.ldy2;
     tiles += q.m_tiles * j.w->n_tiles;
   }
   if (n_jobs == 1) tm[1] = tm[0];
@@ -825,14 +883,47 @@ int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
 int check_job(aex_ctx* ctx, const QmmJob& j) {
   if (j.m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
   if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
+  if (j.glu_tile0 < j.w->n_tiles &&
+      (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8 || gemv_path(j.w, j.m)))
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows on the GEMM path");
   return AEX_OK;
 }
 
 }  // namespace
 
+int qmm_glu_interleave(aex_ctx* ctx, const aex_qweight* src, int plain_rows, int mlp, aex_qweight** out,
+                       cudaStream_t s) {
+  *out = nullptr;
+  if (plain_rows % qmm::kTileN || mlp % 128 || mlp <= 0 || src->n != plain_rows + 2 * mlp)
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "glu interleave: n=%d is not %d plain rows + 2 x %d (128-row multiples)",
+                     src->n, plain_rows, mlp);
+  auto* w = new aex_qweight(*src);
+  w->tiles = nullptr;
+  cudaError_t e = cudaMalloc(&w->tiles, w->bytes);
+  if (e != cudaSuccess) {
+    delete w;
+    return cuda_error(ctx, e, "cudaMalloc(glu interleave)");
+  }
+  const int plain_tiles = plain_rows / qmm::kTileN;
+  qmm::glu_interleave_kernel<<<dim3(src->k_blocks, 2 * src->n_tiles), 256, 0, s>>>(src->tiles, src->k_blocks,
+                                                                                  plain_tiles, mlp, w->tiles);
+  if (int r = check_launch(ctx, "glu_interleave_kernel")) {
+    cudaFree(w->tiles);
+    delete w;
+    return r;
+  }
+  *out = w;
+  return AEX_OK;
+}
+
 int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy, int mode,
             const float* gate, cudaStream_t s) {
   const QmmJob j{w, x, ldx, m, y, ldy, mode, gate};
+  if (int r = check_job(ctx, j)) return r;
+  return run_one(ctx, j, s);
+}
+
+int qmm_run_job(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
   if (int r = check_job(ctx, j)) return r;
   return run_one(ctx, j, s);
 }
