@@ -58,11 +58,27 @@ struct aex_dit {
   float* MOD_TXT = nullptr;   // [6C]
   float* MOD_SINGLE = nullptr;  // [3C]
   float* MOD_OUT = nullptr;   // [2C]
+  float* CUR = nullptr;       // [2] this step's timestep (sigma * 1000) and dt, read by the kernels
+  float* STEPS = nullptr;     // [2 * kMaxGraphSteps] (timestep, dt) per step of a replayed denoise
+  int* STEP_I = nullptr;      // index of the next STEPS entry
   bool rope_set = false, context_set = false, timestep_set = false;
+  // One denoise step (step_select, conditioning, forward, in-place Euler on LATB) captured as a CUDA
+  // graph by aex_dit_denoise and replayed once per step; dropped when weights change.
+  cudaGraphExec_t step_graph = nullptr;
+  cudaStream_t cap_stream = nullptr;  // engine-owned stream the step is captured on (never the legacy stream)
 };
 
 namespace aex {
 namespace {
+
+constexpr int kMaxGraphSteps = 1024;
+
+void drop_graph(aex_dit* d) {
+  if (d->step_graph) {
+    cudaGraphExecDestroy(d->step_graph);
+    d->step_graph = nullptr;
+  }
+}
 
 template <class T>
 int dalloc(aex_dit* d, T** p, size_t count) {
@@ -252,14 +268,68 @@ int single_block(aex_dit* d, int i, cudaStream_t s) {
   return AEX_OK;
 }
 
-int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s) {
-  if (!d->rope_set || !d->context_set || !d->timestep_set)
-    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "set rope, context and timestep before forward");
-  const int C = d->C, lt = d->cfg.l_txt, li = d->cfg.l_img, ic = d->cfg.in_channels;
-  AEX_NEED(xemb, need_lin(d, "x_embedder", C, ic));
-  AEX_NEED(pout, need_lin(d, "proj_out", ic, C));
-  // Fuse the per-stream Q|K|V linears of the double blocks and interleave the gate/up halves of the
-  // feed-forward inputs once.
+// Step conditioning from the timestep in CUR[0] (DirectConditioner.stepConditioning,
+// Sources/ImarelloDirect/DirectConditioner.swift:168-213): sinusoid -> time MLP -> SiLU ->
+// modulation vectors of the double (img, txt), single and output layers.
+int conditioning(aex_dit* d, cudaStream_t s) {
+  const int C = d->C, td = d->cfg.timestep_dim;
+  AEX_NEED(l1, need_lin(d, "time_guidance_embed.linear_1", C, td));
+  AEX_NEED(l2, need_lin(d, "time_guidance_embed.linear_2", C, C));
+  AEX_NEED(mimg, need_lin(d, "double_stream_modulation_img.linear", 6 * C, C));
+  AEX_NEED(mtxt, need_lin(d, "double_stream_modulation_txt.linear", 6 * C, C));
+  AEX_NEED(msin, need_lin(d, "single_stream_modulation.linear", 3 * C, C));
+  AEX_NEED(mout, need_lin(d, "norm_out.linear", 2 * C, C));
+  AEX_TRY(glue::timestep_embedding(d->ctx, d->CUR, td, d->TSIN, s));
+  AEX_TRY(glue::f32_to_bf16(d->ctx, d->TSIN, td, d->TSIN16, s));
+  AEX_TRY(qmm_run(d->ctx, l1, d->TSIN16, td, 1, d->T1, C, 1, nullptr, s));
+  AEX_TRY(glue::silu_to_bf16(d->ctx, d->T1, C, d->T16, s));
+  AEX_TRY(qmm_run(d->ctx, l2, d->T16, C, 1, d->TEMB, C, 1, nullptr, s));
+  AEX_TRY(glue::silu_to_bf16(d->ctx, d->TEMB, C, d->T16, s));
+  AEX_TRY(qmm_run(d->ctx, mimg, d->T16, C, 1, d->MOD_IMG, 6 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, mtxt, d->T16, C, 1, d->MOD_TXT, 6 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, msin, d->T16, C, 1, d->MOD_SINGLE, 3 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run(d->ctx, mout, d->T16, C, 1, d->MOD_OUT, 2 * C, 1, nullptr, s));
+  d->timestep_set = true;
+  return AEX_OK;
+}
+
+int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s);
+
+// One replayable denoise step on LATB in place: scalars of step (*STEP_I)++,
+// conditioning, forward, Euler.
+int graph_step(aex_dit* d, cudaStream_t s) {
+  AEX_TRY(glue::step_select(d->ctx, d->STEPS, d->STEP_I, d->CUR, s));
+  AEX_TRY(conditioning(d, s));
+  AEX_TRY(forward(d, d->LATB, d->PRED, s));
+  return glue::euler(d->ctx, d->LATB, d->PRED, d->CUR + 1,
+                     static_cast<int64_t>(d->cfg.l_img) * d->cfg.in_channels, d->LATB, s);
+}
+
+// Records graph_step (nothing executes) on the engine's own stream; the graph
+// is then launched on the caller's stream.
+int capture_step(aex_dit* d) {
+  if (!d->cap_stream) AEX_CUDA_TRY(d->ctx, cudaStreamCreateWithFlags(&d->cap_stream, cudaStreamNonBlocking));
+  cudaStream_t s = d->cap_stream;
+  AEX_CUDA_TRY(d->ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  const int r = graph_step(d, s);
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (r || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return r ? r : cuda_error(d->ctx, e, "cudaStreamEndCapture(denoise step)");
+  }
+  const cudaError_t ei = cudaGraphInstantiate(&d->step_graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ei != cudaSuccess) {
+    d->step_graph = nullptr;
+    return cuda_error(d->ctx, ei, "cudaGraphInstantiate(denoise step)");
+  }
+  return AEX_OK;
+}
+
+// Derived weights, built once outside any captured step: fused Q|K|V of the
+// double blocks and the gate/up-interleaved feed-forward inputs.
+int prepare_weights(aex_dit* d, cudaStream_t s) {
   for (int i = 0; i < d->cfg.n_double; ++i) {
     AEX_TRY(glu_copy(d, blk("transformer_blocks", i, "ff.linear_in"), 0, s));
     AEX_TRY(glu_copy(d, blk("transformer_blocks", i, "ff_context.linear_in"), 0, s));
@@ -272,6 +342,16 @@ int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s) {
   }
   for (int i = 0; i < d->cfg.n_single; ++i)
     AEX_TRY(glu_copy(d, blk("single_transformer_blocks", i, "attn.to_qkv_mlp_proj"), 3 * d->C, s));
+  return AEX_OK;
+}
+
+int forward(aex_dit* d, const float* latents, float* velocity, cudaStream_t s) {
+  if (!d->rope_set || !d->context_set || !d->timestep_set)
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "set rope, context and timestep before forward");
+  const int C = d->C, lt = d->cfg.l_txt, li = d->cfg.l_img, ic = d->cfg.in_channels;
+  AEX_NEED(xemb, need_lin(d, "x_embedder", C, ic));
+  AEX_NEED(pout, need_lin(d, "proj_out", ic, C));
+  AEX_TRY(prepare_weights(d, s));
   // Embedders: image rows from x_embedder (f32 out), text rows from the projected context.
   AEX_TRY(glue::f32_to_bf16(d->ctx, latents, static_cast<int64_t>(li) * ic, d->LAT16, s));
   AEX_TRY(qmm_run(d->ctx, xemb, d->LAT16, ic, li, d->X + static_cast<int64_t>(lt) * C, C, 1, nullptr, s));
@@ -316,11 +396,11 @@ int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
   const aex_dit_config& c = *cfg;
   if (c.hidden <= 0 || c.heads <= 0 || c.hidden != c.heads * 128)
     return set_error(ctx, AEX_ERR_INVALID_ARG, "hidden must be heads * 128 (head_dim 128)");
-  if (c.n_double < 0 || c.n_single < 0 || c.mlp_hidden <= 0 || c.mlp_hidden % 64 || c.hidden % 256 ||
+  if (c.n_double < 0 || c.n_single < 0 || c.mlp_hidden <= 0 || c.mlp_hidden % 128 || c.hidden % 256 ||
       c.in_channels % 64 || c.text_dim % 64 || c.timestep_dim % 64 || c.l_txt <= 0 || c.l_img <= 0)
     return set_error(ctx, AEX_ERR_INVALID_ARG,
-                     "dims must be positive; hidden a multiple of 256; mlp_hidden, in_channels, text_dim, "
-                     "timestep_dim multiples of 64");
+                     "dims must be positive; hidden a multiple of 256; mlp_hidden of 128; in_channels, "
+                     "text_dim, timestep_dim of 64");
   if (int r = bind_device(ctx)) return r;
   auto* d = new aex_dit();
   d->ctx = ctx;
@@ -354,6 +434,9 @@ int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
   if (!r) r = dalloc(d, &d->MOD_TXT, 6 * C);
   if (!r) r = dalloc(d, &d->MOD_SINGLE, 3 * C);
   if (!r) r = dalloc(d, &d->MOD_OUT, 2 * C);
+  if (!r) r = dalloc(d, &d->CUR, 2);
+  if (!r) r = dalloc(d, &d->STEPS, 2 * static_cast<size_t>(kMaxGraphSteps));
+  if (!r) r = dalloc(d, &d->STEP_I, 1);
   if (r) {
     aex_dit_destroy(d);
     return r;
@@ -366,6 +449,8 @@ void aex_dit_destroy(aex_dit* d) {
   if (!d) return;
   cudaSetDevice(d->ctx->device);
   cudaDeviceSynchronize();
+  aex::drop_graph(d);
+  if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
   for (auto& kv : d->lin) aex_qweight_destroy(kv.second);
   for (auto& kv : d->norms) cudaFree(kv.second);
   for (void* p : d->allocs) cudaFree(p);
@@ -378,6 +463,7 @@ int aex_dit_load_linear(aex_dit* d, const char* name, const uint32_t* packed, co
   if (!d || !name) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
   aex_qweight* w = nullptr;
   if (int r = aex_qweight_create(d->ctx, packed, scales, biases, n, k, 64, 4, &w, stream)) return r;
+  drop_graph(d);
   auto it = d->lin.find(name);
   if (it != d->lin.end()) aex_qweight_destroy(it->second);
   d->lin[name] = w;
@@ -416,6 +502,7 @@ int aex_dit_load_norm(aex_dit* d, const char* name, const float* weight, aex_str
   } else {
     AEX_CUDA_TRY(d->ctx, cudaMalloc(&w, 128 * sizeof(float)));
     d->norms[name] = w;
+    drop_graph(d);
   }
   AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(w, weight, 128 * sizeof(float), cudaMemcpyDeviceToDevice,
                                        static_cast<cudaStream_t>(stream)));
@@ -453,25 +540,8 @@ int aex_dit_set_timestep(aex_dit* d, float timestep, aex_stream stream) {
   if (!d) return set_error(nullptr, AEX_ERR_INVALID_ARG, "NULL dit");
   if (int r = bind_device(d->ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
-  const int C = d->C, td = d->cfg.timestep_dim;
-  AEX_NEED(l1, need_lin(d, "time_guidance_embed.linear_1", C, td));
-  AEX_NEED(l2, need_lin(d, "time_guidance_embed.linear_2", C, C));
-  AEX_NEED(mimg, need_lin(d, "double_stream_modulation_img.linear", 6 * C, C));
-  AEX_NEED(mtxt, need_lin(d, "double_stream_modulation_txt.linear", 6 * C, C));
-  AEX_NEED(msin, need_lin(d, "single_stream_modulation.linear", 3 * C, C));
-  AEX_NEED(mout, need_lin(d, "norm_out.linear", 2 * C, C));
-  AEX_TRY(glue::timestep_embedding(d->ctx, timestep, td, d->TSIN, s));
-  AEX_TRY(glue::f32_to_bf16(d->ctx, d->TSIN, td, d->TSIN16, s));
-  AEX_TRY(qmm_run(d->ctx, l1, d->TSIN16, td, 1, d->T1, C, 1, nullptr, s));
-  AEX_TRY(glue::silu_to_bf16(d->ctx, d->T1, C, d->T16, s));
-  AEX_TRY(qmm_run(d->ctx, l2, d->T16, C, 1, d->TEMB, C, 1, nullptr, s));
-  AEX_TRY(glue::silu_to_bf16(d->ctx, d->TEMB, C, d->T16, s));
-  AEX_TRY(qmm_run(d->ctx, mimg, d->T16, C, 1, d->MOD_IMG, 6 * C, 1, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, mtxt, d->T16, C, 1, d->MOD_TXT, 6 * C, 1, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, msin, d->T16, C, 1, d->MOD_SINGLE, 3 * C, 1, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, mout, d->T16, C, 1, d->MOD_OUT, 2 * C, 1, nullptr, s));
-  d->timestep_set = true;
-  return AEX_OK;
+  AEX_TRY(glue::set_scalar(d->ctx, d->CUR, timestep, s));
+  return conditioning(d, s);
 }
 
 int aex_dit_forward(aex_dit* d, const float* latents, float* velocity, aex_stream stream) {
@@ -486,29 +556,37 @@ int aex_dit_denoise_step(aex_dit* d, const float* lat_in, float* lat_out, float 
   if (!d || !lat_in || !lat_out) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
   if (int r = bind_device(d->ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
+  AEX_TRY(glue::set_scalar(d->ctx, d->CUR + 1, dt, s));
   AEX_TRY(forward(d, lat_in, d->PRED, s));
-  return glue::euler(d->ctx, lat_in, d->PRED, dt, static_cast<int64_t>(d->cfg.l_img) * d->cfg.in_channels, lat_out,
-                     s);
+  return glue::euler(d->ctx, lat_in, d->PRED, d->CUR + 1, static_cast<int64_t>(d->cfg.l_img) * d->cfg.in_channels,
+                     lat_out, s);
 }
 
 int aex_dit_denoise(aex_dit* d, float* latents, int steps, aex_stream stream) {
   using namespace aex;
-  if (!d || !latents || steps < 1) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "bad argument");
+  if (!d || !latents || steps < 1 || steps > kMaxGraphSteps)
+    return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "bad argument (steps in 1..%d)", kMaxGraphSteps);
+  if (!d->rope_set || !d->context_set)
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "set rope and context before denoise");
   if (int r = bind_device(d->ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
   std::vector<float> sig, ts;
   schedule(steps, d->cfg.l_img, sig, ts);
-  float* cur = latents;
-  float* alt = d->LATB;
+  std::vector<float> sc(2 * static_cast<size_t>(steps));
   for (int i = 0; i < steps; ++i) {
-    AEX_TRY(aex_dit_set_timestep(d, ts[i], s));
-    AEX_TRY(aex_dit_denoise_step(d, cur, alt, sig[i + 1] - sig[i], s));
-    std::swap(cur, alt);
+    sc[2 * i] = ts[i];
+    sc[2 * i + 1] = sig[i + 1] - sig[i];
   }
-  if (cur != latents)
-    AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(latents, cur,
-                                         static_cast<size_t>(d->cfg.l_img) * d->cfg.in_channels * sizeof(float),
-                                         cudaMemcpyDeviceToDevice, s));
+  const size_t lat_bytes = static_cast<size_t>(d->cfg.l_img) * d->cfg.in_channels * sizeof(float);
+  // Pageable source: the copy is staged before cudaMemcpyAsync returns, so `sc` may go out of scope.
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->STEPS, sc.data(), sc.size() * sizeof(float), cudaMemcpyHostToDevice, s));
+  AEX_CUDA_TRY(d->ctx, cudaMemsetAsync(d->STEP_I, 0, sizeof(int), s));
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->LATB, latents, lat_bytes, cudaMemcpyDeviceToDevice, s));
+  AEX_TRY(prepare_weights(d, s));
+  d->timestep_set = true;  // the replayed step sets it from STEPS
+  if (!d->step_graph) AEX_TRY(capture_step(d));
+  for (int i = 0; i < steps; ++i) AEX_CUDA_TRY(d->ctx, cudaGraphLaunch(d->step_graph, s));
+  AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(latents, d->LATB, lat_bytes, cudaMemcpyDeviceToDevice, s));
   return AEX_OK;
 }
 

@@ -86,13 +86,16 @@ __global__ void gate_add_kernel(float* __restrict__ x, int64_t ldx, int rows, in
   *xp = fmaf(gate ? gate[c] : 1.f, __uint_as_float(static_cast<uint32_t>(v[r * ldv + c]) << 16) * scale, *xp);
 }
 
-__global__ void euler_kernel(const float* __restrict__ lat_in, const float* __restrict__ v, float dt, int64_t n,
-                             float* __restrict__ lat_out) {
+// In place when lat_out == lat_in (each element reads then writes itself).
+__global__ void euler_kernel(const float* lat_in, const float* __restrict__ v, const float* __restrict__ dt_p,
+                             int64_t n, float* lat_out) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const float dt = *dt_p;
   if (i < n) lat_out[i] = fmaf(dt, v[i], lat_in[i]);
 }
 
-__global__ void timestep_kernel(float t, int dim, float* __restrict__ out) {
+__global__ void timestep_kernel(const float* __restrict__ t_p, int dim, float* __restrict__ out) {
+  const float t = *t_p;
   const int half = dim / 2;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
     const float freq = expf(-logf(10000.0f) * static_cast<float>(i) / static_cast<float>(half));
@@ -101,6 +104,16 @@ __global__ void timestep_kernel(float t, int dim, float* __restrict__ out) {
     out[half + i] = sinf(arg);
   }
   if (dim % 2 && threadIdx.x == 0) out[dim - 1] = 0.f;
+}
+
+__global__ void set_scalar_kernel(float* dst, float v) { *dst = v; }
+
+// cur[0..1] = steps[2i .. 2i+1] for i = (*counter)++ (the per-step scalars of a replayed step).
+__global__ void step_select_kernel(const float* __restrict__ steps, int* counter, float* __restrict__ cur) {
+  const int i = *counter;
+  cur[0] = steps[2 * i];
+  cur[1] = steps[2 * i + 1];
+  *counter = i + 1;
 }
 
 __global__ void silu_to_bf16_kernel(const float* __restrict__ x, int n, uint16_t* __restrict__ y) {
@@ -147,14 +160,25 @@ int gate_add(aex_ctx* ctx, float* x, int64_t ldx, int rows, int C, const float* 
   return check_launch(ctx, "gate_add_kernel");
 }
 
-int euler(aex_ctx* ctx, const float* lat_in, const float* v, float dt, int64_t n, float* lat_out, cudaStream_t s) {
+int euler(aex_ctx* ctx, const float* lat_in, const float* v, const float* dt, int64_t n, float* lat_out,
+          cudaStream_t s) {
   euler_kernel<<<blocks_for(n, 256), 256, 0, s>>>(lat_in, v, dt, n, lat_out);
   return check_launch(ctx, "euler_kernel");
 }
 
-int timestep_embedding(aex_ctx* ctx, float t, int dim, float* out, cudaStream_t s) {
+int timestep_embedding(aex_ctx* ctx, const float* t, int dim, float* out, cudaStream_t s) {
   timestep_kernel<<<1, 128, 0, s>>>(t, dim, out);
   return check_launch(ctx, "timestep_kernel");
+}
+
+int set_scalar(aex_ctx* ctx, float* dst, float v, cudaStream_t s) {
+  set_scalar_kernel<<<1, 1, 0, s>>>(dst, v);
+  return check_launch(ctx, "set_scalar_kernel");
+}
+
+int step_select(aex_ctx* ctx, const float* steps, int* counter, float* cur, cudaStream_t s) {
+  step_select_kernel<<<1, 1, 0, s>>>(steps, counter, cur);
+  return check_launch(ctx, "step_select_kernel");
 }
 
 int silu_to_bf16(aex_ctx* ctx, const float* x, int n, void* y, cudaStream_t s) {

@@ -89,3 +89,35 @@ def test_missing_weight_is_reported(cuda_ctx):
     with pytest.raises(Exception) as e:
         eng.project_context(torch.zeros(CFG.l_txt, CFG.text_dim, dtype=torch.bfloat16, device="cuda"))
     assert "context_embedder" in str(e.value)
+
+
+def _eager_denoise(eng, lat, steps):
+    """The denoise loop issued step by step (set_timestep + denoise_step), no graph."""
+    sig, ts = O.schedule(steps, CFG.l_img)
+    cur, alt = lat.clone(), torch.empty_like(lat)
+    for i in range(steps):
+        eng.set_timestep(float(ts[i]))
+        eng.denoise_step(cur, alt, float(sig[i + 1] - sig[i]))
+        cur, alt = alt, cur
+    return cur
+
+
+def test_graph_replay_matches_eager_and_tracks_weight_reloads(setup, cuda_ctx):
+    """aex_dit_denoise replays one captured step per iteration: twice in a row and
+    against the same loop launched kernel by kernel it must agree bit for bit; after
+    a weight is re-loaded the captured step is rebuilt and still agrees."""
+    eng, ref, lat, e0, cos, sin = setup
+    a = eng.denoise(lat.clone(), steps=3)
+    b = eng.denoise(lat.clone(), steps=3)
+    e = _eager_denoise(eng, lat, 3)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(a, e)
+    lin, _ = dit.random_weights(CFG, seed=99)
+    name = "single_transformer_blocks.1.attn.to_out"
+    eng.load_linear(name, *lin[name])
+    c = eng.denoise(lat.clone(), steps=3)
+    e2 = _eager_denoise(eng, lat, 3)
+    torch.cuda.synchronize()
+    assert not torch.equal(c, a)
+    assert torch.equal(c, e2)
+    assert cuda_ctx.device_status() == 0
