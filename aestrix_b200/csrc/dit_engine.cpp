@@ -69,6 +69,9 @@ struct aex_dit {
 };
 
 namespace aex {
+
+aex_ctx* dit_context(aex_dit* d) { return d->ctx; }
+
 namespace {
 
 constexpr int kMaxGraphSteps = 1024;

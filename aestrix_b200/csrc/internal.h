@@ -99,6 +99,8 @@ int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void*
 int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
                           const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
                           float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream);
+// The context a DiT engine was created on.
+aex_ctx* dit_context(aex_dit* d);
 // Attention (and prep if args ask for it) on validated args.
 int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
                          cudaStream_t stream);

@@ -10,6 +10,7 @@ stepConditioning, DirectConditioner.swift) and ``DirectDiTPackedDenoiser.denoise
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 
 import torch
@@ -155,6 +156,30 @@ class DitEngine:
         """In place: noise in, denoised latents out."""
         self.ctx.check(self.L.aex_dit_denoise(self.handle, latents.data_ptr(), steps, self._s(stream)))
         return latents
+
+    def load_safetensors(self, path, stream=None):
+        """Every 4-bit linear and norm weight of a safetensors file or shard directory
+        (aex_dit_load_safetensors). Returns (linears, norms) loaded."""
+        nl, nn = C.c_int(0), C.c_int(0)
+        self.ctx.check(self.L.aex_dit_load_safetensors(self.handle, os.fspath(path).encode(), C.byref(nl),
+                                                       C.byref(nn), self._s(stream)))
+        return nl.value, nn.value
+
+
+def scan_safetensors(path, max_bytes=1 << 22):
+    """Tensors of a safetensors file or shard directory without the GPU (aex_safetensors_scan):
+    {name: (dtype, shape, file_offset, nbytes)}. Raises AexError for a malformed file."""
+    L = _lib.lib()
+    buf = C.create_string_buffer(max_bytes)
+    rc = L.aex_safetensors_scan(os.fspath(path).encode(), buf, max_bytes)
+    text = buf.value.decode()
+    if rc != 0:
+        raise _lib.AexError(rc, text)
+    out = {}
+    for line in text.splitlines():
+        name, dtype, shape, off, nb = line.split(" ")
+        out[name] = (dtype, tuple(int(v) for v in shape.split(",")) if shape else (), int(off), int(nb))
+    return out
 
 
 def rope_tables(cfg: DitConfig, device="cuda", text_positions="ids", theta=2000.0):

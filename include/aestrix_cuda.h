@@ -257,6 +257,28 @@ int aex_dit_denoise_step(aex_dit* dit, const float* lat_in, float* lat_out, floa
  * the result on return (DirectDiTPackedDenoiser.denoise :25-81). */
 int aex_dit_denoise(aex_dit* dit, float* latents, int steps, aex_stream stream);
 
+/* Weights from MLX safetensors (TransformerWeights.loadQuantized,
+ * Sources/ImarelloDiT/TransformerWeights.swift:13-32; shard discovery as
+ * SafetensorsLoader.shardFileNames, Sources/ImarelloWeights/SafetensorsLoader.swift:6-29;
+ * keys as DirectDiTStep.loadBlocks / loadHead, Sources/ImarelloDirect/DirectDiTStep.swift:278-335,844-884).
+ * `path`: one .safetensors file, or a directory of shards (those named by
+ * model.safetensors.index.json when present, else every *.safetensors, sorted;
+ * a later shard's tensor replaces an earlier one of the same name). Every
+ * "<name>.weight" of dtype U32 [n, k/8] with "<name>.scales" and "<name>.biases"
+ * [n, k/64] (BF16, or F16/F32 holding bf16-exact values) is loaded as the 4-bit
+ * linear <name> (aex_dit_load_linear); every other "<name>.weight" of 128 floats
+ * as the norm weight <name> (aex_dit_load_norm). Any other tensor: AEX_ERR_UNSUPPORTED
+ * naming it. Blocks until the uploads are done. *n_linear / *n_norm (may be NULL)
+ * receive the counts. */
+int aex_dit_load_safetensors(aex_dit* dit, const char* path, int* n_linear, int* n_norm, aex_stream stream);
+
+/* Lists the tensors of a safetensors file or shard directory without touching
+ * the GPU, one line per tensor: "name dtype d0,d1,.. file_offset nbytes\n",
+ * NUL-terminated in out (truncated to out_len). AEX_ERR_INVALID_ARG, with the
+ * reason in out, for a missing, unreadable or malformed file. No reference
+ * counterpart: the inspection side of aex_dit_load_safetensors. */
+int aex_safetensors_scan(const char* path, char* out, size_t out_len);
+
 /* ------------------------------------------------ multi-GPU (NCCL, NVLink) */
 
 /* Sequence-parallel ring attention over P GPUs, one process per GPU. No
