@@ -100,6 +100,39 @@ def scaled_dot_product_attention(query, key, value, scale=None, mask=None, out=N
     return out
 
 
+def rope_tables(ids: torch.Tensor, theta: float = 2000.0, axes_dim=(32, 32, 32, 32), ctx=None, stream=None):
+    """cos/sin [n, sum(axes_dim)/2] f32 on the device of `ids` ([n, len(axes_dim)] f32 CUDA position ids,
+    e.g. text (0,0,0,i), image (t,h,w,0)) through aex_rope_tables (Flux2PosEmbed, PosEmbed.swift:5-48)."""
+    if not (ids.is_cuda and ids.dtype == torch.float32 and ids.is_contiguous() and ids.dim() == 2):
+        raise TypeError("ids must be a contiguous CUDA float32 [n, n_axes] tensor")
+    n = ids.shape[0]
+    half = sum(a // 2 for a in axes_dim)
+    cos = torch.empty(n, half, device=ids.device)
+    sin = torch.empty(n, half, device=ids.device)
+    ctx = ctx or _lib.context(ids.device.index or 0)
+    axes = (C.c_int * len(axes_dim))(*axes_dim)
+    ctx.check(_lib.lib().aex_rope_tables(ctx.handle, ids.data_ptr(), n, C.c_float(theta), axes, len(axes_dim),
+                                         cos.data_ptr(), sin.data_ptr(), _stream_ptr(stream)))
+    return cos, sin
+
+
+def grid_ids(height: int, width: int, t: float = 0.0, device="cuda") -> torch.Tensor:
+    """Image position ids (t, h, w, 0) row-major over the grid (Flux2RoPE.prepareGridIDs)."""
+    hh, ww = torch.meshgrid(torch.arange(height), torch.arange(width), indexing="ij")
+    ids = torch.zeros(height * width, 4, dtype=torch.float32)
+    ids[:, 0] = t
+    ids[:, 1] = hh.reshape(-1).float()
+    ids[:, 2] = ww.reshape(-1).float()
+    return ids.to(device)
+
+
+def text_ids(length: int, device="cuda") -> torch.Tensor:
+    """Text position ids (0, 0, 0, i) (Flux2RoPE.prepareTextIDs)."""
+    ids = torch.zeros(length, 4, dtype=torch.float32)
+    ids[:, 3] = torch.arange(length, dtype=torch.float32)
+    return ids.to(device)
+
+
 def attention_flops(batch: int, seq: int, heads: int, head_dim: int = 128) -> float:
     """Algorithmic FLOPs of one call: two GEMMs of 2*S*S*D per (batch, head)."""
     return 4.0 * batch * heads * seq * seq * head_dim

@@ -345,6 +345,46 @@ def measure_dit(ctx, dev, world, runs=3):
             "config": "BASELINE configs[3]: FLUX.2-klein 1024^2, 4 steps, random-init 4-bit weights, 1 image/GPU"}
 
 
+def measure_i2i(ctx, dev, iters=40):
+    """SURVEY config 5 (i2i): joint attention over 512 text + 64x64 target + 64x64 reference tokens
+    (J = 8,704, 24 x 128, bf16, fused QK-RMSNorm + RoPE; reference ids (10, h, w, 0)), one GPU.
+    Two input sets (each > L2 with the outputs). TFLOP/s counts 4*S^2*D*H = 930.9 GFLOP per call."""
+    import torch
+
+    from aestrix_b200 import attention
+
+    l_txt, grid = 512, 64
+    ids = torch.cat([attention.text_ids(l_txt, dev), attention.grid_ids(grid, grid, 0.0, dev),
+                     attention.grid_ids(grid, grid, 10.0, dev)]).contiguous()
+    S = ids.shape[0]
+    stream = torch.cuda.current_stream(dev)
+    cos, sin = attention.rope_tables(ids, 2000.0, ctx=ctx, stream=stream)
+    g = torch.Generator().manual_seed(55)
+    sets = [tuple(torch.randn(1, S, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+            for _ in range(2)]
+    outs = [torch.empty_like(x[0]) for x in sets]
+    wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    wk = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+
+    def call(i):
+        q, k, v = sets[i % 2]
+        attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, out=outs[i % 2], ctx=ctx, stream=stream)
+
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(iters):
+        call(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    flops = 4.0 * S * S * HEAD_DIM * HEADS
+    return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "gflop_per_call": flops / 1e9, "seq": S,
+            "config": "SURVEY config 5 i2i: 512 text + 4096 target + 4096 reference tokens, fused call"}
+
+
 def measure_ring(ctx, dev, world, rank, iters=5):
     """joint attention at 2048^2 (512 text + 16384 image tokens = 16896, 24 x 128,
     bf16, fused QK-RMSNorm + RoPE), sequence-parallel ring attention over the N GPUs (contiguous shards,
@@ -466,34 +506,55 @@ def run_ours(args):
     ctx.sync(stream.cuda_stream)
 
     # ---- end to end through the C ABI with host buffers (H2D inputs, D2H output per step)
+    # A serving loop: call i's inputs go host -> device on one stream while call i-1 computes and call
+    # i-2's output comes back on another; two device buffer sets. Every call still copies all of its
+    # inputs in (q, k, v, norm weights, RoPE tables) and its output out, from / to pinned host memory.
     hq, hk, hv = (sets[0][j].cpu().pin_memory() for j in range(3))
     hwq, hwk, hcos, hsin = (t.cpu().pin_memory() for t in (wq, wk, cos, sin))
-    ho = torch.empty_like(hq).pin_memory()
-    dq, dk, dv, do = (torch.empty_like(sets[0][j]) for j in range(4))
-    dwq, dwk, dcos, dsin = (torch.empty_like(t) for t in (wq, wk, cos, sin))
+    hos = [torch.empty_like(hq).pin_memory() for _ in range(2)]
+    dev_sets = [[torch.empty_like(t) for t in (sets[0][0], sets[0][1], sets[0][2], wq, wk, cos, sin, sets[0][0])]
+                for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hwq, hwk, hcos, hsin))
-    d2h = ho.numel() * ho.element_size()
+    d2h = hos[0].numel() * hos[0].element_size()
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_cmp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        for d, h in ((dq, hq), (dk, hk), (dv, hv), (dwq, hwq), (dwk, hwk), (dcos, hcos), (dsin, hsin)):
-            d.copy_(h, non_blocking=True)
+    def e2e_step(i):
+        b = i % 2
+        dq, dk, dv, dwq, dwk, dcos, dsin, do = dev_sets[b]
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_cmp[b])  # call i-2 has finished reading this input set
+            for d, h in ((dq, hq), (dk, hk), (dv, hv), (dwq, hwq), (dwk, hwk), (dcos, hcos), (dsin, hsin)):
+                d.copy_(h, non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        if i >= 2:
+            stream.wait_event(ev_out[b])  # call i-2's output has left this buffer
         attention.joint_attention(dq, dk, dv, dwq, dwk, 1e-6, dcos, dsin, out=do, ctx=ctx, stream=stream)
-        ho.copy_(do, non_blocking=True)
+        ev_cmp[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_cmp[b])
+            hos[b].copy_(do, non_blocking=True)
+            ev_out[b].record(s_out)
 
-    for _ in range(2):
-        e2e_step()
+    for i in range(4):
+        e2e_step(i)
     torch.cuda.synchronize()
     _barrier(world)
     ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_e = max(3, min(args.steps, 10))
-    ea.record(stream)
-    for _ in range(n_e):
-        e2e_step()
-    eb.record(stream)
+    n_e = max(4, min(args.steps, 24))
+    ea.record(s_in)
+    for i in range(n_e):
+        e2e_step(i)
+    eb.record(s_out)
     torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(world, ea.elapsed_time(eb) / n_e)
     _barrier(world)
 
+    i2i_res = measure_i2i(ctx, dev)
     qmm_res = measure_qmm(ctx, dev) if not args.no_qmm else None
     dit_res = measure_dit(ctx, dev, world) if not args.no_dit else None
     ring_res = measure_ring(ctx, dev, world, rank) if (world > 1 and not args.no_ring) else None
@@ -515,7 +576,9 @@ def run_ours(args):
                              "seconds": dt_cpu},
             "e2e": {"value": world * FLOPS_PER_CALL / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "path": "aex_joint_attention via ctypes, pinned host buffers, copies on the same stream"},
+                    "path": "aex_joint_attention via ctypes; each call copies its inputs from pinned host memory and "
+                            "its output back; calls pipelined over an H2D stream, the compute stream and a "
+                            "D2H stream with two device buffer sets"},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
@@ -523,6 +586,7 @@ def run_ours(args):
             line["dit_denoise"] = dit_res
         if ring_res is not None:
             line["ring_attention_2048"] = ring_res
+        line["joint_attention_i2i"] = i2i_res
         if qmm_res is not None:
             hbm = _hbm_peak()
             for v in qmm_res.values():

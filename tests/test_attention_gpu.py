@@ -87,6 +87,28 @@ def test_joint_attention_baseline_configs(cuda_ctx, grid, seed):
     _compare(out, ref, rows)
 
 
+# --- i2i (SURVEY config 5): text 512 + target 64x64 + reference 64x64, J = 8,704 -----------------------
+def test_joint_attention_i2i_8704(cuda_ctx):
+    """Image-to-image joint sequence: the reference image's tokens carry ids (10, h, w, 0)
+    (LatentOps.referenceImageIds, Sources/ImarelloCore/LatentOps.swift:41-45) after the target's
+    (0, h, w, 0); sampled query rows against the oracle."""
+    l_txt, grid = 512, 64
+    ids = np.concatenate([O.text_ids(l_txt), O.grid_ids(grid, grid), O.grid_ids(grid, grid, 10.0)], 0)
+    cos, sin = O.rope_freqs(ids, 2000.0)
+    s = ids.shape[0]
+    assert s == 8704
+    q, k, v = _inputs(1, s, 24, 13)
+    wq, wk = _norm_weights(113)
+    out = _run_joint(q, k, v, wq, wk, 1e-6, cos, sin)
+    spans = ((0, 32), (l_txt + grid * grid - 32, l_txt + grid * grid + 32), (s - 32, s))
+    ref = np.full((1, s, 24, 128), np.nan, np.float32)
+    for lo, hi in spans:
+        part = O.joint_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), wq.numpy(), wk.numpy(),
+                                 1e-6, cos, sin, q_begin=lo, q_end=hi)
+        ref[:, lo:hi] = part[:, lo:hi]
+    _compare(out, ref, np.concatenate([np.arange(lo, hi) for lo, hi in spans]))
+
+
 # --- ragged lengths, reference eps / text ids, layouts -------------------------------------------------
 @pytest.mark.parametrize("s", [1, 48, 130, 200, 257, 384, 1000])
 def test_joint_attention_ragged(cuda_ctx, s):
