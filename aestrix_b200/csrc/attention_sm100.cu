@@ -466,57 +466,70 @@ struct PrepParams {
 // Each half-warp owns one 128-wide row (16 lanes x 8 elements = one 16-byte
 // load per lane); a warp keeps kPrepRowsPerWarp rows in flight so every lane
 // has several independent 16-byte loads outstanding (HBM-bound kernel).
-constexpr int kPrepRowsPerWarp = 8;
+#ifndef AEX_PREP_ROWS
+#define AEX_PREP_ROWS 16
+#endif
+constexpr int kPrepRowsPerWarp = AEX_PREP_ROWS;
 constexpr int kPrepWarps = 8;
+
+// Row coordinates (operand, batch, token, head) of a flat row index, advanced
+// incrementally: rows are ordered operand-major, then batch, token, head.
+struct PrepRow {
+  uint32_t which, b, s, h;
+  __device__ __forceinline__ void init(uint32_t row, uint32_t rows_per_op, uint32_t heads, uint32_t seq) {
+    which = row >= rows_per_op ? 1 : 0;
+    const uint32_t r = row - which * rows_per_op;
+    h = r % heads;
+    const uint32_t t = r / heads;
+    s = t % seq;
+    b = t / seq;
+  }
+  __device__ __forceinline__ void advance(uint32_t by, uint32_t heads, uint32_t seq, uint32_t batch) {
+    h += by;
+    while (h >= heads) {  // at most by / heads + 1 rounds
+      h -= heads;
+      if (++s == seq) {
+        s = 0;
+        if (++b == batch) {
+          b = 0;
+          which = 1;
+        }
+      }
+    }
+  }
+};
 
 __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
   // 32-bit index math: the host guarantees 2*B*S*H < 2^31.
   const uint32_t rows_per_op = static_cast<uint32_t>(p.batch) * p.seq * p.heads;
   const uint32_t total = 2 * rows_per_op;
-  const uint32_t heads = p.heads, seq = p.seq;
+  const uint32_t heads = p.heads, seq = p.seq, batch = p.batch;
   const int lane = threadIdx.x & 31;
   const int half = lane >> 4;  // which row of the pair
   const int l16 = lane & 15;   // 8-element slice of the row
-  const uint32_t warp_row0 = (blockIdx.x * kPrepWarps + (threadIdx.x >> 5)) * kPrepRowsPerWarp;
+  const uint32_t row0 = (blockIdx.x * kPrepWarps + (threadIdx.x >> 5)) * kPrepRowsPerWarp + half;
   constexpr int kIt = kPrepRowsPerWarp / 2;
-  // Issue every global load of this thread first (row slices, rotary tables,
-  // norm weights), so their latencies overlap; then compute and store.
+  // Issue every row-slice load of this thread first (kIt x 16 bytes in flight
+  // per lane); rotary tables and norm weights are read at compute time (the
+  // same token's tables serve all its heads, so they hit in L1).
   uint4 raw[kIt];
-  float4 cs[kIt], sn[kIt];
-  int64_t dst_off[kIt];
-  bool valid[kIt];
-  uint32_t which_of[kIt];
-  bool seg_a[kIt];
+  PrepRow c;
+  c.init(row0 < total ? row0 : 0, rows_per_op, heads, seq);
+  const PrepRow c0 = c;
 #pragma unroll
   for (int it = 0; it < kIt; ++it) {
-    const uint32_t row = warp_row0 + 2 * it + half;
-    valid[it] = row < total;
-    const uint32_t rr = valid[it] ? row : 0;
-    const uint32_t which = rr >= rows_per_op ? 1 : 0;
-    const uint32_t r = rr - which * rows_per_op;
-    const int64_t hh = r % heads;
-    const int64_t s = (r / heads) % seq;
-    const int64_t bb = r / (heads * seq);
-    which_of[it] = which;
-    seg_a[it] = s < p.split;
-    const __nv_bfloat16* src = which ? p.k + bb * p.k_sb + s * p.k_ss + hh * p.k_sh
-                                     : p.q + bb * p.q_sb + s * p.q_ss + hh * p.q_sh;
-    raw[it] = valid[it] ? __ldg(reinterpret_cast<const uint4*>(src) + l16) : make_uint4(0, 0, 0, 0);
-    if (p.cos_t) {
-      cs[it] = __ldg(reinterpret_cast<const float4*>(p.cos_t + s * (kD / 2) + l16 * 4));
-      sn[it] = __ldg(reinterpret_cast<const float4*>(p.sin_t + s * (kD / 2) + l16 * 4));
+    raw[it] = make_uint4(0, 0, 0, 0);
+    if (row0 + 2 * it < total) {
+      const __nv_bfloat16* src = c.which ? p.k + c.b * p.k_sb + c.s * p.k_ss + c.h * p.k_sh
+                                         : p.q + c.b * p.q_sb + c.s * p.q_ss + c.h * p.q_sh;
+      raw[it] = __ldg(reinterpret_cast<const uint4*>(src) + l16);
     }
-    dst_off[it] = static_cast<int64_t>(which) * rows_per_op * kD + ((bb * heads + hh) * seq + s) * kD + l16 * 8;
+    c.advance(2, heads, seq, batch);
   }
-  auto load_w = [&](const float* w, float (&d)[8]) {
-    if (w) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(w + l16 * 8));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(w + l16 * 8 + 4));
-      d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
-    }
-  };
+  c = c0;
 #pragma unroll
   for (int it = 0; it < kIt; ++it) {
+    const bool valid = row0 + 2 * it < total;
     float x[8];
     const uint32_t wv4[4] = {raw[it].x, raw[it].y, raw[it].z, raw[it].w};
 #pragma unroll
@@ -531,17 +544,21 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
     for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float* w = which_of[it] ? (seg_a[it] ? p.wk_a : p.wk) : (seg_a[it] ? p.wq_a : p.wq);
+    const bool seg_a = static_cast<int>(c.s) < p.split;
+    const float* w = c.which ? (seg_a ? p.wk_a : p.wk) : (seg_a ? p.wq_a : p.wq);
     if (w) {
-      float wl[8];
-      load_w(w, wl);
+      const float4 wa = __ldg(reinterpret_cast<const float4*>(w + l16 * 8));
+      const float4 wb = __ldg(reinterpret_cast<const float4*>(w + l16 * 8 + 4));
+      const float wl[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
       const float inv = rsqrtf(ss * (1.0f / kD) + p.eps);
 #pragma unroll
       for (int i = 0; i < 8; ++i) x[i] = x[i] * inv * wl[i];
     }
     if (p.cos_t) {
-      const float ca[4] = {cs[it].x, cs[it].y, cs[it].z, cs[it].w};
-      const float sa[4] = {sn[it].x, sn[it].y, sn[it].z, sn[it].w};
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos_t + c.s * (kD / 2) + l16 * 4));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin_t + c.s * (kD / 2) + l16 * 4));
+      const float ca[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float re = x[2 * i], im = x[2 * i + 1];
@@ -549,9 +566,13 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
         x[2 * i + 1] = im * ca[i] + re * sa[i];
       }
     }
-    if (valid[it])
-      *reinterpret_cast<uint4*>(p.out + dst_off[it]) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
-                                                                   pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+    if (valid) {
+      const int64_t dst = static_cast<int64_t>(c.which) * rows_per_op * kD +
+                          (static_cast<int64_t>(c.b * heads + c.h) * seq + c.s) * kD + l16 * 8;
+      *reinterpret_cast<uint4*>(p.out + dst) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                                                          pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+    }
+    c.advance(2, heads, seq, batch);
   }
 }
 
@@ -609,6 +630,7 @@ int bshd_tmap(aex_ctx* ctx, CUtensorMap* m, const void* base, int64_t sb, int64_
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
                    int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
                    float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream) {
+  if (B <= 0 || S <= 0 || H <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "qk prep: empty batch, seq or heads");
   attn::PrepParams pp{};
   pp.q = static_cast<const __nv_bfloat16*>(q);
   pp.k = static_cast<const __nv_bfloat16*>(k);
