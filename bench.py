@@ -31,8 +31,22 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-# stdout carries exactly one JSON line: keep NCCL's own log lines on stderr.
+# stdout carries exactly one JSON line. A private duplicate of the original
+# stdout is kept for it, and file descriptor 1 is pointed at stderr, so that
+# whatever this process or its libraries (NCCL banners, torch warnings) print
+# to stdout lands on stderr.
 os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+_JSON_OUT = os.fdopen(os.dup(1), "w")
+sys.stdout.flush()
+os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    """The one JSON line of this run."""
+    import json
+
+    _JSON_OUT.write(json.dumps(line) + "\n")
+    _JSON_OUT.flush()
 
 import numpy as np  # noqa: E402
 
@@ -257,7 +271,7 @@ def run_reference(args):
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -593,7 +607,7 @@ def run_ours(args):
                 v["frac"] = v["gbs"] / hbm if v["bound"] == "hbm" else v["tflops"] / peak
             line["qmm"] = dict(qmm_res, note="BASELINE configs[2], K=3072; frac of measured HBM GB/s (M=1) or "
                                "measured bf16 TF/s (M>=512)")
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
 
