@@ -111,6 +111,7 @@ _SIGNATURES = [
     ("aex_dit_denoise_step", C.c_int, [_VP, _VP, _VP, C.c_float, _VP]),
     ("aex_dit_denoise", C.c_int, [_VP, _VP, C.c_int, _VP]),
     ("aex_dit_load_safetensors", C.c_int, [_VP, C.c_char_p, _VP, _VP, _VP]),
+    ("aex_dit_set_sequence_parallel", C.c_int, [_VP, _VP, C.c_int, C.c_int]),
     ("aex_safetensors_scan", C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t]),
     ("aex_comm_unique_id", C.c_int, [_VP]),
     ("aex_comm_create", C.c_int, [_VP, C.c_int, C.c_int, _VP, C.c_int, C.POINTER(_VP)]),

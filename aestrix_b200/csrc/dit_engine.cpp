@@ -22,6 +22,7 @@
 // Modulation vectors are [shift | scale | gate] per set (two sets for each
 // double stream, one for the single blocks); norm_out is [scale | shift]
 // (DirectConditioner.stepConditioning :172-213, AdaLayerNormContinuous.swift).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -66,6 +67,11 @@ struct aex_dit {
   // graph by aex_dit_denoise and replayed once per step; dropped when weights change.
   cudaGraphExec_t step_graph = nullptr;
   cudaStream_t cap_stream = nullptr;  // engine-owned stream the step is captured on (never the legacy stream)
+  // Sequence parallelism (aex_dit_set_sequence_parallel): this engine holds one contiguous shard of the
+  // joint sequence; joint attention runs as a ring over `comm`. The scheduler's image length is the
+  // whole image's (l_img_sched).
+  aex_comm* comm = nullptr;
+  int l_img_sched = 0;
 };
 
 namespace aex {
@@ -195,6 +201,42 @@ int attend(aex_dit* d, const uint16_t* v, int64_t v_ld, uint16_t* out, int64_t o
   return joint_attention_impl(d->ctx, &a, nullptr, 0, s);
 }
 
+// One or two GEMM-path jobs in one launch; a job without rows (the text stream
+// of a sequence shard that holds none) is left out.
+int run_jobs(aex_dit* d, const QmmJob& a, const QmmJob& b, cudaStream_t s) {
+  if (a.m <= 0) return b.m > 0 ? qmm_run_job(d->ctx, b, s) : AEX_OK;
+  if (b.m <= 0) return qmm_run_job(d->ctx, a, s);
+  return qmm_run2(d->ctx, a, b, s);
+}
+
+int ln_mod_rows(aex_dit* d, const float* x, int rows, const float* scale, const float* shift, uint16_t* y,
+                cudaStream_t s) {
+  if (rows <= 0) return AEX_OK;
+  return glue::ln_mod(d->ctx, x, d->C, rows, d->C, scale, shift, d->cfg.ln_eps, y, d->C, s);
+}
+
+// QK-RMSNorm + RoPE of the Q, K columns of PROJ (row pitch ld; rows < split
+// use the (wq_a, wk_a) weights) and the joint attention with V into out: on
+// this GPU, or as a ring over the sequence shards of all ranks.
+int joint_attend(aex_dit* d, int64_t ld, const float* wq, const float* wk, const float* wq_a, const float* wk_a,
+                 int split, uint16_t* out, int64_t out_ld, cudaStream_t s) {
+  const int J = d->J, H = d->H, C = d->C;
+  const int64_t qs[3] = {static_cast<int64_t>(J) * ld, ld, 128};
+  const uint16_t* v = d->PROJ + 2 * C;
+  if (d->comm) {
+    uint16_t *Q = nullptr, *K0 = nullptr, *V0 = nullptr;
+    AEX_TRY(ring_buffers(d->ctx, d->comm, J, H, &Q, &K0, &V0));
+    AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, H, wq, wk, wq_a, wk_a, split, d->cfg.rms_eps,
+                           d->COS, d->SIN, Q, s));
+    AEX_CUDA_TRY(d->ctx, cudaMemcpy2DAsync(V0, static_cast<size_t>(H) * 256, v, static_cast<size_t>(ld) * 2,
+                                           static_cast<size_t>(H) * 256, J, cudaMemcpyDeviceToDevice, s));
+    return ring_run(d->ctx, d->comm, J, H, 1.0f / std::sqrt(128.0f), out, out_ld, 128, s);
+  }
+  AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, H, wq, wk, wq_a, wk_a, split, d->cfg.rms_eps,
+                         d->COS, d->SIN, d->PREP, s));
+  return attend(d, v, ld, out, out_ld, s);
+}
+
 int double_block(aex_dit* d, int i, cudaStream_t s) {
   const int C = d->C, J = d->J, lt = d->cfg.l_txt, li = d->cfg.l_img, mlp = d->mlp;
   const float eps_ln = d->cfg.ln_eps;
@@ -217,21 +259,18 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   AEX_NEED(naq, need_norm(d, blk("transformer_blocks", i, "attn.norm_added_q")));
   AEX_NEED(nak, need_norm(d, blk("transformer_blocks", i, "attn.norm_added_k")));
   // attention half
-  AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + C, mt, eps_ln, NHt, C, s));
-  AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + C, mi, eps_ln, NHi, C, s));
+  AEX_TRY(ln_mod_rows(d, Xt, lt, mt + C, mt, NHt, s));
+  AEX_TRY(ln_mod_rows(d, Xi, li, mi + C, mi, NHi, s));
   const int64_t pq = 3 * C;  // PROJ row pitch for Q|K|V
   // Each text-stream linear shares one launch with its image-stream twin.
-  AEX_TRY(qmm_run2(d->ctx, QmmJob{qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr},
+  AEX_TRY(run_jobs(d, QmmJob{qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr},
                    QmmJob{qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr}, s));
-  const int64_t qs[3] = {static_cast<int64_t>(J) * pq, pq, 128};
-  AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, d->H, nq, nk, naq, nak, lt, d->cfg.rms_eps, d->COS,
-                         d->SIN, d->PREP, s));
-  AEX_TRY(attend(d, d->PROJ + 2 * C, pq, d->ATT, C, s));
-  AEX_TRY(qmm_run2(d->ctx, QmmJob{out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C},
+  AEX_TRY(joint_attend(d, pq, nq, nk, naq, nak, lt, d->ATT, C, s));
+  AEX_TRY(run_jobs(d, QmmJob{out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C},
                    QmmJob{out_i, d->ATT + static_cast<int64_t>(lt) * C, C, li, Xi, C, 2, mi + 2 * C}, s));
   // MLP half (per stream)
-  AEX_TRY(glue::ln_mod(d->ctx, Xt, C, lt, C, mt + 4 * C, mt + 3 * C, eps_ln, NHt, C, s));
-  AEX_TRY(glue::ln_mod(d->ctx, Xi, C, li, C, mi + 4 * C, mi + 3 * C, eps_ln, NHi, C, s));
+  AEX_TRY(ln_mod_rows(d, Xt, lt, mt + 4 * C, mt + 3 * C, NHt, s));
+  AEX_TRY(ln_mod_rows(d, Xi, li, mi + 4 * C, mi + 3 * C, NHi, s));
   uint16_t* SWt = d->ATT;                                   // [lt, mlp]
   uint16_t* SWi = d->ATT + static_cast<int64_t>(lt) * mlp;  // [li, mlp]
   // linear_in with the SwiGLU in its epilogue (gate/up interleaved weights): silu(g) * u straight into SW.
@@ -241,14 +280,14 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   ff_t.y2 = SWt;
   ff_i.y2 = SWi;
   ff_t.ldy2 = ff_i.ldy2 = mlp;
-  AEX_TRY(qmm_run2(d->ctx, ff_t, ff_i, s));
-  AEX_TRY(qmm_run2(d->ctx, QmmJob{ffo_t, SWt, mlp, lt, Xt, C, 2, mt + 5 * C},
+  AEX_TRY(run_jobs(d, ff_t, ff_i, s));
+  AEX_TRY(run_jobs(d, QmmJob{ffo_t, SWt, mlp, lt, Xt, C, 2, mt + 5 * C},
                    QmmJob{ffo_i, SWi, mlp, li, Xi, C, 2, mi + 5 * C}, s));
   return AEX_OK;
 }
 
 int single_block(aex_dit* d, int i, cudaStream_t s) {
-  const int C = d->C, J = d->J, mlp = d->mlp;
+  const int C = d->C, J = d->J;
   AEX_NEED(proj, need_lin(d, blk("single_transformer_blocks", i, "attn.to_qkv_mlp_proj#glu"), d->proj, C));
   AEX_NEED(out, need_lin(d, blk("single_transformer_blocks", i, "attn.to_out"), C, d->cat));
   AEX_NEED(nq, need_norm(d, blk("single_transformer_blocks", i, "attn.norm_q")));
@@ -263,10 +302,7 @@ int single_block(aex_dit* d, int i, cudaStream_t s) {
   pj.y2 = d->ATT + C;
   pj.ldy2 = d->cat;
   AEX_TRY(qmm_run_job(d->ctx, pj, s));
-  const int64_t qs[3] = {static_cast<int64_t>(J) * pp, pp, 128};
-  AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, d->H, nq, nk, nullptr, nullptr, 0,
-                         d->cfg.rms_eps, d->COS, d->SIN, d->PREP, s));
-  AEX_TRY(attend(d, d->PROJ + 2 * C, pp, d->ATT, d->cat, s));
+  AEX_TRY(joint_attend(d, pp, nq, nk, nullptr, nullptr, 0, d->ATT, d->cat, s));
   AEX_TRY(qmm_run(d->ctx, out, d->ATT, d->cat, J, d->X, C, 2, ms + 2 * C, s));
   return AEX_OK;
 }
@@ -400,7 +436,7 @@ int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
   if (c.hidden <= 0 || c.heads <= 0 || c.hidden != c.heads * 128)
     return set_error(ctx, AEX_ERR_INVALID_ARG, "hidden must be heads * 128 (head_dim 128)");
   if (c.n_double < 0 || c.n_single < 0 || c.mlp_hidden <= 0 || c.mlp_hidden % 128 || c.hidden % 256 ||
-      c.in_channels % 64 || c.text_dim % 64 || c.timestep_dim % 64 || c.l_txt <= 0 || c.l_img <= 0)
+      c.in_channels % 64 || c.text_dim % 64 || c.timestep_dim % 64 || c.l_txt < 0 || c.l_img <= 0)
     return set_error(ctx, AEX_ERR_INVALID_ARG,
                      "dims must be positive; hidden a multiple of 256; mlp_hidden of 128; in_channels, "
                      "text_dim, timestep_dim of 64");
@@ -411,6 +447,7 @@ int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
   d->C = c.hidden;
   d->H = c.heads;
   d->J = c.l_txt + c.l_img;
+  d->l_img_sched = c.l_img;
   d->mlp = c.mlp_hidden;
   d->proj = 3 * c.hidden + 2 * c.mlp_hidden;
   d->cat = c.hidden + c.mlp_hidden;
@@ -418,7 +455,7 @@ int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
   const size_t proj_w = std::max<size_t>(d->proj, 2 * static_cast<size_t>(d->mlp));
   int r = AEX_OK;
   if (!r) r = dalloc(d, &d->X, J * C);
-  if (!r) r = dalloc(d, &d->E0, static_cast<size_t>(c.l_txt) * C);
+  if (!r) r = dalloc(d, &d->E0, static_cast<size_t>(std::max(c.l_txt, 1)) * C);
   if (!r) r = dalloc(d, &d->NH, J * C);
   if (!r) r = dalloc(d, &d->PROJ, J * proj_w);
   if (!r) r = dalloc(d, &d->ATT, J * static_cast<size_t>(d->cat));
@@ -530,6 +567,10 @@ int aex_dit_project_context(aex_dit* d, const void* embeds, aex_stream stream) {
   if (int r = bind_device(d->ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
   const int C = d->C, lt = d->cfg.l_txt;
+  if (lt == 0) {  // a sequence shard without text rows
+    d->context_set = true;
+    return AEX_OK;
+  }
   AEX_NEED(ctxemb, need_lin(d, "context_embedder", C, d->cfg.text_dim));
   // bf16 output (the reference's bf16 qmm), widened to the f32 text residual.
   AEX_TRY(qmm_run(d->ctx, ctxemb, embeds, d->cfg.text_dim, lt, d->NH, C, 0, nullptr, s));
@@ -574,7 +615,7 @@ int aex_dit_denoise(aex_dit* d, float* latents, int steps, aex_stream stream) {
   if (int r = bind_device(d->ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
   std::vector<float> sig, ts;
-  schedule(steps, d->cfg.l_img, sig, ts);
+  schedule(steps, d->l_img_sched, sig, ts);
   std::vector<float> sc(2 * static_cast<size_t>(steps));
   for (int i = 0; i < steps; ++i) {
     sc[2 * i] = ts[i];
@@ -587,9 +628,38 @@ int aex_dit_denoise(aex_dit* d, float* latents, int steps, aex_stream stream) {
   AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(d->LATB, latents, lat_bytes, cudaMemcpyDeviceToDevice, s));
   AEX_TRY(prepare_weights(d, s));
   d->timestep_set = true;  // the replayed step sets it from STEPS
-  if (!d->step_graph) AEX_TRY(capture_step(d));
-  for (int i = 0; i < steps; ++i) AEX_CUDA_TRY(d->ctx, cudaGraphLaunch(d->step_graph, s));
+  if (d->comm) {
+    // Sequence-parallel steps exchange K/V over NCCL on a side stream: launched step by step.
+    for (int i = 0; i < steps; ++i) AEX_TRY(graph_step(d, s));
+  } else {
+    if (!d->step_graph) AEX_TRY(capture_step(d));
+    for (int i = 0; i < steps; ++i) AEX_CUDA_TRY(d->ctx, cudaGraphLaunch(d->step_graph, s));
+  }
   AEX_CUDA_TRY(d->ctx, cudaMemcpyAsync(latents, d->LATB, lat_bytes, cudaMemcpyDeviceToDevice, s));
+  return AEX_OK;
+}
+
+int aex_dit_set_sequence_parallel(aex_dit* d, aex_comm* comm, int l_txt_total, int l_img_total) {
+  using namespace aex;
+  if (!d) return set_error(nullptr, AEX_ERR_INVALID_ARG, "NULL dit");
+  drop_graph(d);
+  if (!comm) {
+    d->comm = nullptr;
+    d->l_img_sched = d->cfg.l_img;
+    return AEX_OK;
+  }
+  const int P = comm_world(comm), r = comm_rank(comm);
+  const int64_t J_total = static_cast<int64_t>(l_txt_total) + l_img_total;
+  if (l_txt_total < 0 || l_img_total <= 0 || J_total % P || J_total / P != d->J)
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG,
+                     "sequence shards must be equal: %lld joint rows over %d ranks, this engine holds %d",
+                     static_cast<long long>(J_total), P, d->J);
+  if ((r == 0 && d->cfg.l_txt != l_txt_total) || (r > 0 && d->cfg.l_txt != 0))
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG,
+                     "the text rows (%d) must all be on rank 0: this rank (%d) holds %d", l_txt_total, r,
+                     d->cfg.l_txt);
+  d->comm = comm;
+  d->l_img_sched = l_img_total;
   return AEX_OK;
 }
 

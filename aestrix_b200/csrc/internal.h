@@ -99,6 +99,18 @@ int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void*
 int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
                           const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
                           float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream);
+// Ring attention internals (ring_attention.cpp) for callers that prepare Q/K
+// themselves: the local Q plane and K ring slot 0 (head-major [H][S][128],
+// adjacent, as written by launch_qk_prep) and V ring slot 0 (token-major
+// [S][H*128]) of this communicator's ring state, grown to S rows of H heads;
+// then the hop loop over all ranks (joint attention of the local queries
+// against every rank's K/V, merged by log-sum-exp) into out (bf16, strides
+// in elements: token, head).
+int ring_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, uint16_t** q, uint16_t** k0, uint16_t** v0);
+int comm_world(const aex_comm* c);
+int comm_rank(const aex_comm* c);
+int ring_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
+             cudaStream_t s);
 // The context a DiT engine was created on.
 aex_ctx* dit_context(aex_dit* d);
 // Attention (and prep if args ask for it) on validated args.

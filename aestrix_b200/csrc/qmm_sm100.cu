@@ -867,10 +867,12 @@ int launch_gemm_pair(aex_ctx* ctx, const QmmJob* jobs, int n_jobs, cudaStream_t 
 }
 
 bool gemv_path(const aex_qweight* w, int m) { return m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps; }
+// The GEMV has no SwiGLU epilogue: jobs that need it take the GEMM at any m.
+bool use_gemv(const QmmJob& j) { return gemv_path(j.w, j.m) && j.glu_tile0 >= j.w->n_tiles; }
 
 int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
   const aex_qweight* w = j.w;
-  if (gemv_path(w, j.m)) {
+  if (use_gemv(j)) {
     if (j.m <= 1) return launch_gemv<1>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
     if (j.m <= 2) return launch_gemv<2>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
     if (j.m <= 4) return launch_gemv<4>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
@@ -883,9 +885,8 @@ int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
 int check_job(aex_ctx* ctx, const QmmJob& j) {
   if (j.m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
   if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
-  if (j.glu_tile0 < j.w->n_tiles &&
-      (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8 || gemv_path(j.w, j.m)))
-    return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows on the GEMM path");
+  if (j.glu_tile0 < j.w->n_tiles && (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8))
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows");
   return AEX_OK;
 }
 
@@ -931,7 +932,7 @@ int qmm_run_job(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
 int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s) {
   if (int r = check_job(ctx, a)) return r;
   if (int r = check_job(ctx, b)) return r;
-  if (!gemv_path(a.w, a.m) && !gemv_path(b.w, b.m)) {
+  if (!use_gemv(a) && !use_gemv(b)) {
     const QmmJob jobs[2] = {a, b};
     return launch_gemm_pair(ctx, jobs, 2, s);
   }

@@ -111,6 +111,92 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace
 }  // namespace aex
 
+namespace aex {
+
+int comm_world(const aex_comm* c) { return c->world; }
+int comm_rank(const aex_comm* c) { return c->rank; }
+
+int ring_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, uint16_t** q, uint16_t** k0, uint16_t** v0) {
+  if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
+  const size_t plane = static_cast<size_t>(H) * S * 128;
+  // Layout of the ring state: Q plane | K ring[2] (head-major) | V ring[2] (token-major) |
+  // O_h bf16 | O_acc f32 | lse_h | lse ping-pong[2]. Q and K ring[0] are adjacent (one prep writes both).
+  const size_t bq = align256(plane * 2), bkv = align256(plane * 2), bo = align256(plane * 2),
+               bacc = align256(plane * 4), blse = align256(static_cast<size_t>(H) * S * 4);
+  if (bq != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
+  const size_t off_k = bq, off_v = off_k + 2 * bkv, off_o = off_v + 2 * bkv, off_acc = off_o + bo,
+               off_lh = off_acc + bacc, off_l0 = off_lh + blse, total = off_l0 + 2 * blse;
+  if (int e = grow(c, total)) return e;
+  uint8_t* base = static_cast<uint8_t*>(c->buf);
+  *q = reinterpret_cast<uint16_t*>(base);
+  *k0 = reinterpret_cast<uint16_t*>(base + off_k);
+  *v0 = reinterpret_cast<uint16_t*>(base + off_v);
+  return AEX_OK;
+}
+
+int ring_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
+             cudaStream_t s) {
+  const int P = c->world, r = c->rank;
+  const size_t plane = static_cast<size_t>(H) * S * 128;  // elements of one [H][S][128] or [S][H][128] block
+  const size_t bq = align256(plane * 2), bkv = align256(plane * 2), bo = align256(plane * 2),
+               bacc = align256(plane * 4), blse = align256(static_cast<size_t>(H) * S * 4);
+  const size_t off_q = 0, off_k = bq, off_v = off_k + 2 * bkv, off_o = off_v + 2 * bkv, off_acc = off_o + bo,
+               off_lh = off_acc + bacc, off_l0 = off_lh + blse;
+  uint8_t* base = static_cast<uint8_t*>(c->buf);
+  uint16_t* Q = reinterpret_cast<uint16_t*>(base + off_q);
+  uint16_t* Kr[2] = {reinterpret_cast<uint16_t*>(base + off_k), reinterpret_cast<uint16_t*>(base + off_k + bkv)};
+  uint16_t* Vr[2] = {reinterpret_cast<uint16_t*>(base + off_v), reinterpret_cast<uint16_t*>(base + off_v + bkv)};
+  uint16_t* Oh = reinterpret_cast<uint16_t*>(base + off_o);
+  float* Oacc = reinterpret_cast<float*>(base + off_acc);
+  float* lse_h = reinterpret_cast<float*>(base + off_lh);
+  float* lse_acc[2] = {reinterpret_cast<float*>(base + off_l0), reinterpret_cast<float*>(base + off_l0 + blse)};
+  AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_start, s));
+  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_start, 0));
+  const int64_t q_st[3] = {static_cast<int64_t>(plane), 128, static_cast<int64_t>(S) * 128};   // head-major
+  const int64_t v_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};  // token-major
+  const int64_t o_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};
+  const size_t kv_bytes = plane * 2;
+  const int next = (r + 1) % P, prev = (r - 1 + P) % P;
+  for (int hop = 0; hop < P; ++hop) {
+    const int cur = hop & 1, nxt = cur ^ 1;
+    if (hop + 1 < P) {
+      // Exchange on the ring stream: send the shard in hand, receive the next one.
+      if (hop > 0) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_attn[nxt], 0));  // nxt no longer read
+      ncclResult_t nr = nccl().groupStart();
+      if (nr == ncclSuccess) nr = nccl().send(Kr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
+      if (nr == ncclSuccess) nr = nccl().send(Vr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
+      if (nr == ncclSuccess) nr = nccl().recv(Kr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
+      if (nr == ncclSuccess) nr = nccl().recv(Vr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
+      ncclResult_t ne = nccl().groupEnd();
+      if (nr != ncclSuccess && nr != ncclInProgress) return nccl_error(ctx, nr, "ncclSend/ncclRecv");
+      // Non-blocking communicator: wait (bounded) until the group is enqueued on the stream.
+      const auto t0 = std::chrono::steady_clock::now();
+      while (ne == ncclInProgress) {
+        ncclResult_t st = ncclInProgress;
+        const ncclResult_t q = nccl().commGetAsyncError(c->comm, &st);
+        if (q != ncclSuccess) return nccl_error(ctx, q, "ncclCommGetAsyncError");
+        ne = st;
+        if (ne == ncclInProgress && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30))
+          return set_error(ctx, AEX_ERR_TIMEOUT, "NCCL group not enqueued after 30 s");
+      }
+      if (ne != ncclSuccess) return nccl_error(ctx, ne, "ncclGroupEnd");
+      AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_recv, c->stream));
+    }
+    // Attention of the local queries against the shard in hand, then merge.
+    if (int e = launch_attention_core(ctx, Q, q_st, Kr[cur], q_st, Vr[cur], v_st, Oh, o_st, 1, S, S, H, scale,
+                                      lse_h, 0, S, s))
+      return e;
+    AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_attn[cur], s));
+    if (int e = ring::merge(ctx, Oh, static_cast<int64_t>(H) * 128, 128, lse_h, lse_acc[hop & 1],
+                            lse_acc[(hop + 1) & 1], Oacc, S, H, hop == 0, hop == P - 1, out, out_ss, out_sh, s))
+      return e;
+    if (hop + 1 < P) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(s, c->ev_recv, 0));
+  }
+  return AEX_OK;
+}
+
+}  // namespace aex
+
 extern "C" {
 
 int aex_comm_unique_id(void* id_out) {
@@ -199,82 +285,24 @@ int aex_ring_attention(aex_ctx* ctx, aex_comm* c, const aex_attention_args* a, a
   if (a->head_dim != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "head_dim must be 128");
   if (a->batch != 1) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention takes batch 1");
   if (a->seq <= 0 || a->heads <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "seq/heads must be positive");
+  if (a->v.stride_h != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention needs V heads contiguous");
   if (int r = bind_device(ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
-  const int P = c->world, r = c->rank, S = a->seq, H = a->heads;
-  const size_t plane = static_cast<size_t>(H) * S * 128;  // elements of one [H][S][128] or [S][H][128] block
-  // Layout of the ring state: Q plane | K ring[2] (head-major) | V ring[2] (token-major) |
-  // O_h bf16 | O_acc f32 | lse_h | lse ping-pong[2].
-  const size_t bq = align256(plane * 2), bkv = align256(plane * 2), bo = align256(plane * 2),
-               bacc = align256(plane * 4), blse = align256(static_cast<size_t>(H) * S * 4);
-  const size_t off_q = 0, off_k = bq, off_v = off_k + 2 * bkv, off_o = off_v + 2 * bkv, off_acc = off_o + bo,
-               off_lh = off_acc + bacc, off_l0 = off_lh + blse, total = off_l0 + 2 * blse;
-  if (int e = grow(c, total)) return e;
-  uint8_t* base = static_cast<uint8_t*>(c->buf);
-  uint16_t* Q = reinterpret_cast<uint16_t*>(base + off_q);
-  uint16_t* Kr[2] = {reinterpret_cast<uint16_t*>(base + off_k), reinterpret_cast<uint16_t*>(base + off_k + bkv)};
-  uint16_t* Vr[2] = {reinterpret_cast<uint16_t*>(base + off_v), reinterpret_cast<uint16_t*>(base + off_v + bkv)};
-  uint16_t* Oh = reinterpret_cast<uint16_t*>(base + off_o);
-  float* Oacc = reinterpret_cast<float*>(base + off_acc);
-  float* lse_h = reinterpret_cast<float*>(base + off_lh);
-  float* lse_acc[2] = {reinterpret_cast<float*>(base + off_l0), reinterpret_cast<float*>(base + off_l0 + blse)};
+  const int S = a->seq, H = a->heads;
+  uint16_t *Q = nullptr, *K0 = nullptr, *V0 = nullptr;
+  if (int e = ring_buffers(ctx, c, S, H, &Q, &K0, &V0)) return e;
   // 1. This rank's Q and K: norm + RoPE (rows of the local shard) straight into Q and K ring[0]
   //    (the prep writes the Q plane, then the K plane, contiguously; K ring[0] follows Q).
   const int64_t qs[3] = {a->q.stride_b, a->q.stride_s, a->q.stride_h};
   const int64_t ks[3] = {a->k.stride_b, a->k.stride_s, a->k.stride_h};
-  if (bq != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
   if (int e = launch_qk_prep(ctx, a->q.data, qs, a->k.data, ks, 1, S, H, a->norm_q_weight, a->norm_k_weight, nullptr,
                              nullptr, 0, a->eps, a->rope_cos, a->rope_sin, Q, s))
     return e;
   // 2. This rank's V into V ring[0] (token-major, contiguous rows of H*128).
-  AEX_CUDA_TRY(ctx, cudaMemcpy2DAsync(Vr[0], static_cast<size_t>(H) * 256, a->v.data,
+  AEX_CUDA_TRY(ctx, cudaMemcpy2DAsync(V0, static_cast<size_t>(H) * 256, a->v.data,
                                       static_cast<size_t>(a->v.stride_s) * 2, static_cast<size_t>(H) * 256, S,
                                       cudaMemcpyDeviceToDevice, s));
-  if (a->v.stride_h != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention needs V heads contiguous");
-  AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_start, s));
-  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_start, 0));
-  const int64_t q_st[3] = {static_cast<int64_t>(plane), 128, static_cast<int64_t>(S) * 128};   // head-major
-  const int64_t v_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};  // token-major
-  const int64_t o_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};
-  const size_t kv_bytes = plane * 2;
-  const int next = (r + 1) % P, prev = (r - 1 + P) % P;
-  for (int hop = 0; hop < P; ++hop) {
-    const int cur = hop & 1, nxt = cur ^ 1;
-    if (hop + 1 < P) {
-      // Exchange on the ring stream: send the shard in hand, receive the next one.
-      if (hop > 0) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_attn[nxt], 0));  // nxt no longer read
-      ncclResult_t nr = nccl().groupStart();
-      if (nr == ncclSuccess) nr = nccl().send(Kr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
-      if (nr == ncclSuccess) nr = nccl().send(Vr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
-      if (nr == ncclSuccess) nr = nccl().recv(Kr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
-      if (nr == ncclSuccess) nr = nccl().recv(Vr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
-      ncclResult_t ne = nccl().groupEnd();
-      if (nr != ncclSuccess && nr != ncclInProgress) return nccl_error(ctx, nr, "ncclSend/ncclRecv");
-      // Non-blocking communicator: wait (bounded) until the group is enqueued on the stream.
-      const auto t0 = std::chrono::steady_clock::now();
-      while (ne == ncclInProgress) {
-        ncclResult_t st = ncclInProgress;
-        const ncclResult_t q = nccl().commGetAsyncError(c->comm, &st);
-        if (q != ncclSuccess) return nccl_error(ctx, q, "ncclCommGetAsyncError");
-        ne = st;
-        if (ne == ncclInProgress && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30))
-          return set_error(ctx, AEX_ERR_TIMEOUT, "NCCL group not enqueued after 30 s");
-      }
-      if (ne != ncclSuccess) return nccl_error(ctx, ne, "ncclGroupEnd");
-      AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_recv, c->stream));
-    }
-    // Attention of the local queries against the shard in hand, then merge.
-    if (int e = launch_attention_core(ctx, Q, q_st, Kr[cur], q_st, Vr[cur], v_st, Oh, o_st, 1, S, S, H, a->scale,
-                                      lse_h, 0, S, s))
-      return e;
-    AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_attn[cur], s));
-    if (int e = ring::merge(ctx, Oh, static_cast<int64_t>(H) * 128, 128, lse_h, lse_acc[hop & 1],
-                            lse_acc[(hop + 1) & 1], Oacc, S, H, hop == 0, hop == P - 1, a->out.data, a->out.stride_s,
-                            a->out.stride_h, s))
-      return e;
-    if (hop + 1 < P) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(s, c->ev_recv, 0));
-  }
-  return AEX_OK;
+  return ring_run(ctx, c, S, H, a->scale, a->out.data, a->out.stride_s, a->out.stride_h, s);
 }
 
 }  // extern "C"

@@ -157,6 +157,11 @@ class DitEngine:
         self.ctx.check(self.L.aex_dit_denoise(self.handle, latents.data_ptr(), steps, self._s(stream)))
         return latents
 
+    def set_sequence_parallel(self, comm, l_txt_total: int, l_img_total: int):
+        """This engine holds one contiguous shard of the joint sequence; joint attention runs as a
+        ring over `comm` (an aex_comm handle, or None to return to one GPU)."""
+        self.ctx.check(self.L.aex_dit_set_sequence_parallel(self.handle, comm, l_txt_total, l_img_total))
+
     def load_safetensors(self, path, stream=None):
         """Every 4-bit linear and norm weight of a safetensors file or shard directory
         (aex_dit_load_safetensors). Returns (linears, norms) loaded."""

@@ -302,6 +302,19 @@ int aex_comm_abort(aex_comm* comm);
  * contiguous. Every rank calls it with the same shapes. */
 int aex_ring_attention(aex_ctx* ctx, aex_comm* comm, const aex_attention_args* args, aex_stream stream);
 
+/* Sequence parallelism for one image over the ranks of `comm` (SURVEY config 5,
+ * 2048^2; ImarelloPipeline.swift:921-927 drives one GPU per image): this engine
+ * was created for one contiguous shard of the joint sequence (cfg.l_txt +
+ * cfg.l_img = (l_txt_total + l_img_total) / world rows; all text rows on rank 0,
+ * cfg.l_txt = 0 elsewhere; RoPE tables and latents are the shard's rows). Linears
+ * and glue stay on the shard; each block's joint attention runs as a ring over
+ * all ranks (aex_ring_attention's schedule, NCCL point-to-point); the scheduler
+ * uses l_img_total. Every rank makes the same calls in the same order.
+ * aex_dit_denoise then launches its steps one by one (no CUDA graph). comm NULL
+ * returns the engine to one GPU. */
+int aex_dit_set_sequence_parallel(aex_dit* dit, aex_comm* comm, int l_txt_total, int l_img_total);
+
+
 /* -------------------------------------------------------------- self test */
 
 /* Tensor-core path self test (no reference counterpart; a device bring-up
