@@ -359,6 +359,88 @@ def measure_dit(ctx, dev, world, runs=3):
             "config": "BASELINE configs[3]: FLUX.2-klein 1024^2, 4 steps, random-init 4-bit weights, 1 image/GPU"}
 
 
+def _make_comm(ctx, dev, world, rank):
+    """An aex_comm over all ranks (unique id broadcast over the torch process group)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from aestrix_b200 import _lib
+
+    L = _lib.lib()
+    uid = (C.c_char * 128)()
+    if rank == 0:
+        ctx.check(L.aex_comm_unique_id(uid))
+    t = torch.frombuffer(bytearray(bytes(uid)), dtype=torch.uint8).to(dev)
+    dist.broadcast(t, src=0)
+    uid = (C.c_char * 128).from_buffer_copy(bytes(t.cpu().numpy()))
+    comm = C.c_void_p()
+    ctx.check(L.aex_comm_create(ctx.handle, world, rank, uid, 120000, C.byref(comm)))
+    return comm
+
+
+def measure_dit_sp(ctx, dev, world, rank, runs=2):
+    """SURVEY config 5 at the DiT level: the 4-step FLUX.2-klein denoise of ONE 2048^2 image (512 text +
+    128x128 image tokens, J = 16,896) sequence-parallel over the N GPUs (aex_dit_set_sequence_parallel:
+    contiguous shards of J/N tokens, text on rank 0, each block's joint attention as a ring over NCCL).
+    Random-init 4-bit weights as configs[3]. Device time of aex_dit_denoise, max over ranks; TFLOP/s
+    counts the whole image's linears and attention."""
+    import torch
+
+    from aestrix_b200 import _lib, attention, dit
+
+    l_txt, grid = 512, 128
+    full = dit.DitConfig(l_txt=l_txt, l_img=grid * grid)
+    J = full.seq
+    if J % world or J // world < l_txt:
+        return {"skipped": f"{J} tokens do not split into {world} shards of at least {l_txt}"}
+    Jp = J // world
+    r0 = rank * Jp
+    lt = max(0, min(l_txt, r0 + Jp) - r0)
+    li = Jp - lt
+    img0 = r0 + lt - l_txt
+    cfg = dit.DitConfig(l_txt=lt, l_img=li)
+    lin, norms = dit.random_weights(cfg, seed=11, device=dev)  # same values on every rank
+    eng = dit.DitEngine(cfg, ctx=ctx, device=dev.index)
+    eng.load(lin, norms)
+    del lin
+    ids = torch.cat([attention.text_ids(l_txt, dev), attention.grid_ids(grid, grid, 0.0, dev)]).contiguous()
+    cos, sin = attention.rope_tables(ids, 2000.0, ctx=ctx)
+    eng.set_rope(cos[r0:r0 + Jp].contiguous(), sin[r0:r0 + Jp].contiguous())
+    g = torch.Generator().manual_seed(99)
+    embeds = torch.randn(l_txt, full.text_dim, generator=g).to(torch.bfloat16).to(dev)
+    eng.project_context(embeds)
+    comm = _make_comm(ctx, dev, world, rank)
+    eng.set_sequence_parallel(comm, l_txt, grid * grid)
+    noise = torch.randn(grid * grid, full.in_channels, generator=torch.Generator().manual_seed(42))
+    noise = noise[img0:img0 + li].contiguous().to(dev)
+    lat = noise.clone()
+    eng.denoise(lat, steps=4)  # warm-up
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    times = []
+    for _ in range(runs):
+        lat.copy_(noise)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        eng.denoise(lat, steps=4, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = _max_over_ranks(world, min(times))
+    ok = bool(torch.isfinite(lat).all().item())
+    eng.close()
+    _lib.lib().aex_comm_destroy(comm)
+    fl = dit.dit_flops(full)
+    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12,
+            "tflop_per_step": fl["total"] / 1e12, "shard_tokens": Jp, "n_gpus": world, "finite": ok,
+            "config": "SURVEY config 5: FLUX.2-klein 2048^2 (J=16,896), 4 steps, one image sequence-parallel "
+                      "over the GPUs, random-init 4-bit weights"}
+
+
 def measure_i2i(ctx, dev, iters=40):
     """SURVEY config 5 (i2i): joint attention over 512 text + 64x64 target + 64x64 reference tokens
     (J = 8,704, 24 x 128, bf16, fused QK-RMSNorm + RoPE; reference ids (10, h, w, 0)), one GPU.
@@ -416,14 +498,7 @@ def measure_ring(ctx, dev, world, rank, iters=5):
         return {"skipped": f"sequence {S} not divisible by {world}"}
     Sp = S // world
     L = _lib.lib()
-    uid = (C.c_char * 128)()
-    if rank == 0:
-        ctx.check(L.aex_comm_unique_id(uid))
-    t = torch.frombuffer(bytearray(bytes(uid)), dtype=torch.uint8).to(dev)
-    dist.broadcast(t, src=0)
-    uid = (C.c_char * 128).from_buffer_copy(bytes(t.cpu().numpy()))
-    comm = C.c_void_p()
-    ctx.check(L.aex_comm_create(ctx.handle, world, rank, uid, 120000, C.byref(comm)))
+    comm = _make_comm(ctx, dev, world, rank)
     g = torch.Generator().manual_seed(77 + rank)
     q, k, v = (torch.randn(1, Sp, H, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
     wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
@@ -572,6 +647,7 @@ def run_ours(args):
     qmm_res = measure_qmm(ctx, dev) if not args.no_qmm else None
     dit_res = measure_dit(ctx, dev, world) if not args.no_dit else None
     ring_res = measure_ring(ctx, dev, world, rank) if (world > 1 and not args.no_ring) else None
+    sp_res = measure_dit_sp(ctx, dev, world, rank) if (world > 1 and not args.no_ring and not args.no_dit) else None
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = FLOPS_PER_CALL / (kernel_ms * 1e-3) / 1e12
@@ -601,6 +677,8 @@ def run_ours(args):
         if ring_res is not None:
             line["ring_attention_2048"] = ring_res
         line["joint_attention_i2i"] = i2i_res
+        if sp_res is not None:
+            line["dit_denoise_2048_sequence_parallel"] = sp_res
         if qmm_res is not None:
             hbm = _hbm_peak()
             for v in qmm_res.values():
@@ -625,7 +703,7 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=90.0, help="target duration of the reference arm")
     ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 4-step DiT denoise measurement")
-    ap.add_argument("--no-ring", action="store_true", help="skip the 2048^2 ring attention measurement (N > 1)")
+    ap.add_argument("--no-ring", action="store_true", help="skip the 2048^2 ring attention and sequence-parallel denoise measurements (N > 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
