@@ -666,10 +666,36 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   }
   // 2. Stage this split's x slice as f32, then per-group sums (one warp per
   //    (row, group) pair, shuffle-reduced).
-  for (int i = t; i < R * nkb * kKB; i += kGemvRows) {
-    const int mr = i / (nkb * kKB), kk = i % (nkb * kKB);
-    xs[mr * kbps * kKB + kk] =
-        mr < p.m ? bf16_bits_to_f32(p.x[static_cast<int64_t>(mr) * p.ldx + kb0 * kKB + kk]) : 0.f;
+  //    8 bf16 per 16-byte load (ldx % 8 == 0 and x 16-byte aligned, checked on the host), every
+  //    load of a thread issued before its stores.
+  {
+    constexpr int kMaxVec = (R * kGemvMaxKbps * kKB / 8 + kGemvRows - 1) / kGemvRows;
+    const int per_row = nkb * kKB / 8, nvec = R * per_row;
+    uint4 xv[kMaxVec];
+#pragma unroll
+    for (int j = 0; j < kMaxVec; ++j) {
+      const int i = t + j * kGemvRows;
+      xv[j] = make_uint4(0, 0, 0, 0);
+      if (i < nvec) {
+        const int mr = i / per_row, c8 = i % per_row;
+        if (mr < p.m)
+          xv[j] = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c8);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxVec; ++j) {
+      const int i = t + j * kGemvRows;
+      if (i < nvec) {
+        const int mr = i / per_row, c8 = i % per_row;
+        float* d = xs + mr * kbps * kKB + c8 * 8;
+        const uint32_t u[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          d[2 * e] = bf16lo_to_f32(u[e]);
+          d[2 * e + 1] = bf16hi_to_f32(u[e]);
+        }
+      }
+    }
   }
   __syncthreads();
   {
@@ -702,19 +728,26 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t t = code_pair_128(ws[c], i);  // codes 2i, 2i+1 of the (permuted) word
-          const float2 q = fadd2(make_float2(__uint_as_float(t << 16), __uint_as_float(t & 0xFFFF0000u)),
-                                 make_float2(-128.0f, -128.0f));
-          const int kk = g * kKB + c * 8 + 2 * i;  // codes kk, kk+1
+        for (int i = 0; i < 4; i += 2) {
+          // codes 2i .. 2i+3 of the (permuted) word as f32 128 + q; the offset is removed once per
+          // group below (sum x (128 + q) - 128 sum x: products exact, sums in f32)
+          const uint32_t t0 = code_pair_128(ws[c], i), t1 = code_pair_128(ws[c], i + 1);
+          const float2 q0 = make_float2(__uint_as_float(t0 << 16), __uint_as_float(t0 & 0xFFFF0000u));
+          const float2 q1 = make_float2(__uint_as_float(t1 << 16), __uint_as_float(t1 & 0xFFFF0000u));
+          const int kk = g * kKB + c * 8 + 2 * i;  // codes kk .. kk+3
 #pragma unroll
-          for (int mr = 0; mr < R; ++mr)
-            tq[mr] = ffma2(q, *reinterpret_cast<const float2*>(xs + mr * kbps * kKB + kk), tq[mr]);
+          for (int mr = 0; mr < R; ++mr) {
+            const float4 x4 = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
+            tq[mr] = ffma2(q0, make_float2(x4.x, x4.y), tq[mr]);
+            tq[mr] = ffma2(q1, make_float2(x4.z, x4.w), tq[mr]);
+          }
         }
       }
 #pragma unroll
-      for (int mr = 0; mr < R; ++mr)
-        acc[mr] = fmaf(sc, tq[mr].x + tq[mr].y, fmaf(bi, gsum[mr * kbps + g], acc[mr]));
+      for (int mr = 0; mr < R; ++mr) {
+        const float gs = gsum[mr * kbps + g];
+        acc[mr] = fmaf(sc, fmaf(-128.0f, gs, tq[mr].x + tq[mr].y), fmaf(bi, gs, acc[mr]));
+      }
     }
   }
 #pragma unroll
@@ -723,10 +756,16 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   cluster_sync_all();
   if (cluster_ctarank() == 0 && active) {
     const uint32_t my_part = smem_u32(part);
+    const int nsplit = static_cast<int>(gridDim.y);
     for (int mr = 0; mr < R && mr < p.m; ++mr) {
+      // every remote load first, then the sum in split order
+      float pv[kGemvMaxSplit];
+#pragma unroll
+      for (int c = 0; c < kGemvMaxSplit; ++c)
+        pv[c] = c < nsplit ? ld_shared_cluster_f32(mapa_shared(my_part + (mr * kGemvRows + t) * 4, c)) : 0.f;
       float v = 0.f;
-      for (int c = 0; c < static_cast<int>(gridDim.y); ++c)
-        v += ld_shared_cluster_f32(mapa_shared(my_part + (mr * kGemvRows + t) * 4, c));
+#pragma unroll
+      for (int c = 0; c < kGemvMaxSplit; ++c) v += pv[c];
       if (p.mode == kOutResidualGate)
         static_cast<float*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] += p.gate[row] * v;
       else if (p.mode == kOutF32)
@@ -884,6 +923,8 @@ int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
 
 int check_job(aex_ctx* ctx, const QmmJob& j) {
   if (j.m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
+  if ((reinterpret_cast<uintptr_t>(j.x) & 15) || j.ldx % 8 || j.ldx < j.w->k)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "x must be 16-byte aligned with ldx >= k and ldx %% 8 == 0");
   if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
   if (j.glu_tile0 < j.w->n_tiles && (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8))
     return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows");
