@@ -275,10 +275,12 @@ def run_reference(args):
     return 0
 
 
-def measure_qmm(ctx, dev, iters=20):
+def measure_qmm(ctx, dev, iters=60):
     """4-bit affine linears 3072 -> 9216 (QKV) and 3072 -> 18432 (SwiGLU) at
     M in {4608, 512, 1}. Weights rotate over enough device copies to exceed L2 (> 160 MB), so every
-    call streams its weight from HBM. TFLOP/s = 2*M*N*K / time; GB/s = algorithmic bytes
+    call streams its weight from HBM. The timed calls (one per weight copy, repeated) are replayed
+    from a CUDA graph, so the device time of back-to-back calls is measured without the host's
+    per-call cost (which exceeds a 10 us GEMV). TFLOP/s = 2*M*N*K / time; GB/s = algorithmic bytes
     (N*K/2 packed + N*K/64*4 bf16 scale+bias + 2*M*K x + 2*M*N y) / time."""
     import torch
 
@@ -295,15 +297,28 @@ def measure_qmm(ctx, dev, iters=20):
         for M in (4608, 512, 1):
             x = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).to(torch.bfloat16).to(dev)
             y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-            for i in range(3):
-                ws[i % copies](x, out=y, stream=stream)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for i in range(iters):
-                ws[i % copies](x, out=y, stream=stream)
-            e1.record(stream)
+            gs = torch.cuda.Stream(dev)
+            with torch.cuda.stream(gs):
+                for i in range(3):
+                    ws[i % copies](x, out=y, stream=gs)
             torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / iters
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=gs):
+                for i in range(copies):
+                    ws[i % copies](x, out=y, stream=gs)
+            torch.cuda.synchronize()
+            graph.replay()
+            torch.cuda.synchronize()
+            reps = max(1, iters // copies)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(gs)
+            with torch.cuda.stream(gs):
+                for _ in range(reps):
+                    graph.replay()
+            e1.record(gs)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / (reps * copies)
+            del graph
             nbytes = wbytes + 2 * M * K + 2 * M * N
             out[f"M{M}_N{N}"] = {"ms": ms, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
                                  "gbs": nbytes / (ms * 1e-3) / 1e9,
