@@ -23,9 +23,11 @@
 //     output tiles, persistent over up to two problems per launch; the
 //     weights are dequantized in registers into the 128-byte swizzled K-major
 //     bf16 B tile (see the kernel's comment for the roles and the pipeline).
-//     gemv_kernel<R> — R <= 16 activation rows, HBM-bound: one thread per
-//     weight row, split-K over a thread-block cluster, partial sums reduced
-//     through distributed shared memory (no scratch, no atomics). The dot uses
+//     gemv_kernel<R> — R <= 16 activation rows, HBM-bound: per CTA 128 weight
+//     rows (one chunk half) and one K split of a thread-block cluster; the
+//     half-chunks are bulk-copied into shared memory, one thread per weight row
+//     computes, partial sums are reduced through distributed shared memory (no
+//     scratch, no atomics). The dot uses
 //     y = sum_g scale_g * (sum_{k in g} x_k q_k) + bias_g * (sum_{k in g} x_k)
 //     (f32), i.e. the unrounded dequantized weights.
 #include <algorithm>
@@ -619,9 +621,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 }
 
 // ------------------------------------------------------------------ GEMV
-constexpr int kGemvRows = 128;     // weight rows (outputs) per CTA, one per thread
+// A CTA owns 128 weight rows (outputs) — exactly one half of a 256-row tile, so
+// its weights for a K block are one contiguous 4608-byte half-chunk — and one
+// K split of the cluster. Thread 0 bulk-copies every half-chunk of the split
+// into shared memory at once (one mbarrier per K block; the copy engine keeps
+// HBM busy without per-thread loads in flight), the threads stage x meanwhile
+// and then take the K blocks in order as they land, one weight row each.
+// Partial sums of the cluster's splits are reduced in CTA rank 0 through
+// distributed shared memory (no scratch, no atomics, fixed order).
+constexpr int kGemvRows = 128;
 constexpr int kGemvMaxSplit = 8;   // cluster size along K (portable limit)
-constexpr int kGemvMaxKbps = 8;    // K blocks per CTA (weights prefetched into registers)
+constexpr int kGemvMaxKbps = 8;    // K blocks per CTA
 
 struct GemvParams {
   const uint16_t* x;  // bf16 [m, ldx]
@@ -632,42 +642,50 @@ struct GemvParams {
   int64_t ldy;
   int mode;
   const float* gate;
+  int* status;
 };
+
+// Shared memory of gemv_kernel<R> for `kbps` K blocks per CTA.
+__host__ __device__ constexpr size_t gemv_smem_bytes(int R, int kbps) {
+  return static_cast<size_t>(kbps) * kHalfBytes                                   // weight half-chunks
+         + static_cast<size_t>(R) * (kbps * kKB + kbps + kGemvRows) * 4          // x, group sums, partials
+         + 8 + static_cast<size_t>(kbps) * 8;                                    // align + barriers
+}
 
 template <int R>
 __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
-  extern __shared__ float gsm[];  // x slice [R][kbps*64] f32, group sums [R][kbps], partials [R][128]
+  extern __shared__ __align__(16) uint8_t gsm_raw[];
   const int kbps = p.kb_per_split;
-  float* xs = gsm;
+  uint8_t* wsm = gsm_raw;
+  float* xs = reinterpret_cast<float*>(gsm_raw + static_cast<size_t>(kbps) * kHalfBytes);
   float* gsum = xs + R * kbps * kKB;
   float* part = gsum + R * kbps;
+  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(part + R * kGemvRows) + 7) & ~uintptr_t(7));
+  __shared__ int abort_flag;
   const int t = threadIdx.x;
   const int split = blockIdx.y;
   const int kb0 = split * kbps;
   const int kb1 = min(p.k_blocks, kb0 + kbps);
   const int nkb = max(0, kb1 - kb0);
   const int row = blockIdx.x * kGemvRows + t;  // weight row (output column)
-  const int nt = row / kTileN, r = row % kTileN;
+  const int nt = blockIdx.x >> 1, half = blockIdx.x & 1;
   const bool active = row < p.n;
-  // 1. Issue every weight load of this thread's K range (kGemvMaxKbps blocks
-  //    of 32 packed bytes + scale + bias) before anything else, so the HBM
-  //    fetch overlaps the x staging below.
-  uint4 wv[2 * kGemvMaxKbps];
-  uint16_t sv[kGemvMaxKbps], bv[kGemvMaxKbps];
-#pragma unroll
-  for (int g = 0; g < kGemvMaxKbps; ++g) {
-    if (active && g < nkb) {
-      const uint8_t* chunk = p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks);
-      wv[2 * g] = __ldg(reinterpret_cast<const uint4*>(chunk + pk_off(r)));
-      wv[2 * g + 1] = __ldg(reinterpret_cast<const uint4*>(chunk + pk_off(r)) + 1);
-      sv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + sc_off(r)));
-      bv[g] = __ldg(reinterpret_cast<const uint16_t*>(chunk + bi_off(r)));
+  // 1. Barriers, then every weight copy of this CTA's K range.
+  if (t == 0) {
+    abort_flag = 0;
+    for (int g = 0; g < nkb; ++g) mbar_init(&bars[g], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (t == 0) {
+    for (int g = 0; g < nkb; ++g) {
+      mbar_arrive_expect_tx(&bars[g], kHalfBytes);
+      bulk_load(wsm + g * kHalfBytes, p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes, kHalfBytes,
+                &bars[g]);
     }
   }
-  // 2. Stage this split's x slice as f32, then per-group sums (one warp per
-  //    (row, group) pair, shuffle-reduced).
-  //    8 bf16 per 16-byte load (ldx % 8 == 0 and x 16-byte aligned, checked on the host), every
-  //    load of a thread issued before its stores.
+  // 2. Stage this split's x slice as f32 (16-byte loads: ldx % 8 == 0 and x 16-byte aligned, checked on
+  //    the host; every load of a thread issued before its stores), then per-group sums.
   {
     constexpr int kMaxVec = (R * kGemvMaxKbps * kKB / 8 + kGemvRows - 1) / kGemvRows;
     const int per_row = nkb * kKB / 8, nvec = R * per_row;
@@ -710,43 +728,55 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
     }
   }
   __syncthreads();
-  // 3. Dot products: y_m += scale * sum_k(x_mk * q_k) + bias * sum_k(x_mk) per group.
+  // 3. Dot products per group as its weights land: y_m += scale * sum_k(x_mk * q_k) +
+  //    bias * sum_k(x_mk), the unrounded dequantized weights. The codes enter as exact f32 (128 + q)
+  //    and the offset is removed once per group (sum x (128 + q) - 128 sum x; products exact, f32 sums).
   float acc[R];
 #pragma unroll
   for (int mr = 0; mr < R; ++mr) acc[mr] = 0.f;
-  if (active) {
+  int landed = 0;
+  for (int g = 0; g < nkb; ++g) {
+    if (!mbar_wait(&bars[g], 0, &abort_flag, p.status, kDevTimeoutTma)) break;
+    landed = g + 1;
+    if (!active) continue;
+    const uint8_t* hb = wsm + g * kHalfBytes;
+    const uint4 w0 = *reinterpret_cast<const uint4*>(hb + t * 32);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(hb + t * 32 + 16);
+    const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4096 + t * 2));
+    const float bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4352 + t * 2));
+    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float2 tq[R];
 #pragma unroll
-    for (int g = 0; g < kGemvMaxKbps; ++g) {
-      if (g >= nkb) break;
-      const float sc = bf16_bits_to_f32(sv[g]);
-      const float bi = bf16_bits_to_f32(bv[g]);
-      const uint32_t ws[8] = {wv[2 * g].x, wv[2 * g].y, wv[2 * g].z, wv[2 * g].w,
-                              wv[2 * g + 1].x, wv[2 * g + 1].y, wv[2 * g + 1].z, wv[2 * g + 1].w};
-      float2 tq[R];
+    for (int mr = 0; mr < R; ++mr) tq[mr] = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int mr = 0; mr < R; ++mr) tq[mr] = make_float2(0.f, 0.f);
+    for (int c = 0; c < 8; ++c) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int i = 0; i < 4; i += 2) {
+        // codes 2i .. 2i+3 of the (permuted) word as f32 128 + q
+        const uint32_t t0 = code_pair_128(ws[c], i), t1 = code_pair_128(ws[c], i + 1);
+        const float2 q0 = make_float2(__uint_as_float(t0 << 16), __uint_as_float(t0 & 0xFFFF0000u));
+        const float2 q1 = make_float2(__uint_as_float(t1 << 16), __uint_as_float(t1 & 0xFFFF0000u));
+        const int kk = g * kKB + c * 8 + 2 * i;  // codes kk .. kk+3
 #pragma unroll
-        for (int i = 0; i < 4; i += 2) {
-          // codes 2i .. 2i+3 of the (permuted) word as f32 128 + q; the offset is removed once per
-          // group below (sum x (128 + q) - 128 sum x: products exact, sums in f32)
-          const uint32_t t0 = code_pair_128(ws[c], i), t1 = code_pair_128(ws[c], i + 1);
-          const float2 q0 = make_float2(__uint_as_float(t0 << 16), __uint_as_float(t0 & 0xFFFF0000u));
-          const float2 q1 = make_float2(__uint_as_float(t1 << 16), __uint_as_float(t1 & 0xFFFF0000u));
-          const int kk = g * kKB + c * 8 + 2 * i;  // codes kk .. kk+3
-#pragma unroll
-          for (int mr = 0; mr < R; ++mr) {
-            const float4 x4 = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
-            tq[mr] = ffma2(q0, make_float2(x4.x, x4.y), tq[mr]);
-            tq[mr] = ffma2(q1, make_float2(x4.z, x4.w), tq[mr]);
-          }
+        for (int mr = 0; mr < R; ++mr) {
+          const float4 x4 = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
+          tq[mr] = ffma2(q0, make_float2(x4.x, x4.y), tq[mr]);
+          tq[mr] = ffma2(q1, make_float2(x4.z, x4.w), tq[mr]);
         }
       }
+    }
 #pragma unroll
-      for (int mr = 0; mr < R; ++mr) {
-        const float gs = gsum[mr * kbps + g];
-        acc[mr] = fmaf(sc, fmaf(-128.0f, gs, tq[mr].x + tq[mr].y), fmaf(bi, gs, acc[mr]));
+    for (int mr = 0; mr < R; ++mr) {
+      const float gs = gsum[mr * kbps + g];
+      acc[mr] = fmaf(sc, fmaf(-128.0f, gs, tq[mr].x + tq[mr].y), fmaf(bi, gs, acc[mr]));
+    }
+  }
+  if (landed < nkb && t == 0) {
+    // Aborting: let the copies still in flight land before the CTA can exit.
+    for (int g = landed; g < nkb; ++g) {
+      const uint32_t a = smem_u32(&bars[g]);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
       }
     }
   }
@@ -808,14 +838,15 @@ int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
   split = std::min(split, w->k_blocks);
   int kbps = (w->k_blocks + split - 1) / split;
   // x slice + group sums + partials in dynamic shared memory (<= 200 KB).
-  auto smem_for = [&](int kb) { return static_cast<size_t>(R) * (kb * 64 + kb + qmm::kGemvRows) * 4; };
+  auto smem_for = [&](int kb) { return qmm::gemv_smem_bytes(R, kb); };
   constexpr size_t kMaxSmem = 200 * 1024;
   if (smem_for(kbps) > kMaxSmem)
     return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w->k, R);
   split = (w->k_blocks + kbps - 1) / kbps;
   AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(qmm::gemv_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kMaxSmem)));
-  qmm::GemvParams p{static_cast<const uint16_t*>(x), ldx, w->tiles, m, w->n, w->k_blocks, kbps, y, ldy, mode, gate};
+  qmm::GemvParams p{static_cast<const uint16_t*>(x), ldx, w->tiles, m, w->n, w->k_blocks, kbps, y, ldy, mode, gate,
+                    ctx->d_status};
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(n_ctas, split, 1);
   cfg.blockDim = dim3(qmm::kGemvRows, 1, 1);
