@@ -215,25 +215,44 @@ int ln_mod_rows(aex_dit* d, const float* x, int rows, const float* scale, const 
   return glue::ln_mod(d->ctx, x, d->C, rows, d->C, scale, shift, d->cfg.ln_eps, y, d->C, s);
 }
 
-// QK-RMSNorm + RoPE of the Q, K columns of PROJ (row pitch ld; rows < split
-// use the (wq_a, wk_a) weights) and the joint attention with V into out: on
-// this GPU, or as a ring over the sequence shards of all ranks.
-int joint_attend(aex_dit* d, int64_t ld, const float* wq, const float* wk, const float* wq_a, const float* wk_a,
-                 int split, uint16_t* out, int64_t out_ld, cudaStream_t s) {
+// Where the Q|K projections go after QK-RMSNorm + RoPE (the QKV GEMM's
+// epilogue writes them): head-major [2][H][J][128], this GPU's PREP buffer or,
+// sequence-parallel, the local Q / K ring slot 0 of the ring state.
+int qk_destination(aex_dit* d, uint16_t** dst) {
+  if (d->comm) {
+    uint16_t *K0 = nullptr, *V0 = nullptr;
+    return ring_buffers(d->ctx, d->comm, d->J, d->H, dst, &K0, &V0);
+  }
+  *dst = d->PREP;
+  return AEX_OK;
+}
+
+// A QKV job with the QK-RMSNorm + RoPE epilogue for rows [tok0, tok0 + m) of the joint sequence.
+void with_qk_prep(aex_dit* d, QmmJob& j, uint16_t* prep, int tok0, const float* wq, const float* wk) {
+  j.qk_tiles = d->H;
+  j.prep = prep;
+  j.tok0 = tok0;
+  j.j_total = d->J;
+  j.h_total = d->H;
+  j.norm_q = wq;
+  j.norm_k = wk;
+  j.eps = d->cfg.rms_eps;
+  j.rope_cos = d->COS;
+  j.rope_sin = d->SIN;
+}
+
+// Joint attention on the prepared Q / K (qk_destination) and the V columns of PROJ (row pitch ld) into out:
+// on this GPU, or as a ring over the sequence shards of all ranks.
+int joint_attend(aex_dit* d, int64_t ld, uint16_t* out, int64_t out_ld, cudaStream_t s) {
   const int J = d->J, H = d->H, C = d->C;
-  const int64_t qs[3] = {static_cast<int64_t>(J) * ld, ld, 128};
   const uint16_t* v = d->PROJ + 2 * C;
   if (d->comm) {
     uint16_t *Q = nullptr, *K0 = nullptr, *V0 = nullptr;
     AEX_TRY(ring_buffers(d->ctx, d->comm, J, H, &Q, &K0, &V0));
-    AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, H, wq, wk, wq_a, wk_a, split, d->cfg.rms_eps,
-                           d->COS, d->SIN, Q, s));
     AEX_CUDA_TRY(d->ctx, cudaMemcpy2DAsync(V0, static_cast<size_t>(H) * 256, v, static_cast<size_t>(ld) * 2,
                                            static_cast<size_t>(H) * 256, J, cudaMemcpyDeviceToDevice, s));
     return ring_run(d->ctx, d->comm, J, H, 1.0f / std::sqrt(128.0f), out, out_ld, 128, s);
   }
-  AEX_TRY(launch_qk_prep(d->ctx, d->PROJ, qs, d->PROJ + C, qs, 1, J, H, wq, wk, wq_a, wk_a, split, d->cfg.rms_eps,
-                         d->COS, d->SIN, d->PREP, s));
   return attend(d, v, ld, out, out_ld, s);
 }
 
@@ -262,10 +281,16 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   AEX_TRY(ln_mod_rows(d, Xt, lt, mt + C, mt, NHt, s));
   AEX_TRY(ln_mod_rows(d, Xi, li, mi + C, mi, NHi, s));
   const int64_t pq = 3 * C;  // PROJ row pitch for Q|K|V
-  // Each text-stream linear shares one launch with its image-stream twin.
-  AEX_TRY(run_jobs(d, QmmJob{qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr},
-                   QmmJob{qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr}, s));
-  AEX_TRY(joint_attend(d, pq, nq, nk, naq, nak, lt, d->ATT, C, s));
+  // Each text-stream linear shares one launch with its image-stream twin. Q and K leave the GEMM normalized
+  // and rotated (per-stream norm weights: norm_added_* on text rows, norm_* on image rows); V goes to PROJ.
+  uint16_t* prep = nullptr;
+  AEX_TRY(qk_destination(d, &prep));
+  QmmJob jt{qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr};
+  QmmJob ji{qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr};
+  with_qk_prep(d, jt, prep, 0, naq, nak);
+  with_qk_prep(d, ji, prep, lt, nq, nk);
+  AEX_TRY(run_jobs(d, jt, ji, s));
+  AEX_TRY(joint_attend(d, pq, d->ATT, C, s));
   AEX_TRY(run_jobs(d, QmmJob{out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C},
                    QmmJob{out_i, d->ATT + static_cast<int64_t>(lt) * C, C, li, Xi, C, 2, mi + 2 * C}, s));
   // MLP half (per stream)
@@ -301,8 +326,11 @@ int single_block(aex_dit* d, int i, cudaStream_t s) {
   pj.glu_tile0 = 3 * C / 256;
   pj.y2 = d->ATT + C;
   pj.ldy2 = d->cat;
+  uint16_t* prep = nullptr;
+  AEX_TRY(qk_destination(d, &prep));
+  with_qk_prep(d, pj, prep, 0, nq, nk);  // Q, K normalized and rotated in the epilogue
   AEX_TRY(qmm_run_job(d->ctx, pj, s));
-  AEX_TRY(joint_attend(d, pp, nq, nk, nullptr, nullptr, 0, d->ATT, d->cat, s));
+  AEX_TRY(joint_attend(d, pp, d->ATT, d->cat, s));
   AEX_TRY(qmm_run(d->ctx, out, d->ATT, d->cat, J, d->X, C, 2, ms + 2 * C, s));
   return AEX_OK;
 }

@@ -80,6 +80,19 @@ struct QmmJob {
   int glu_tile0 = 1 << 30;
   uint16_t* y2 = nullptr;
   int64_t ldy2 = 0;
+  // Weight tiles before qk_tiles are the Q then K projections of h_total heads
+  // (qk_tiles = h_total: two heads per 256-row tile): their output goes through
+  // QK-RMSNorm (norm_q / norm_k, eps; NULL: none) + RoPE (rope_cos / rope_sin
+  // [j_total, 64]; NULL: none) into prep [2][h_total][j_total][128], row r of
+  // this job being token tok0 + r.
+  int qk_tiles = 0;
+  uint16_t* prep = nullptr;
+  int tok0 = 0, j_total = 0, h_total = 0;
+  const float* norm_q = nullptr;
+  const float* norm_k = nullptr;
+  float eps = 0.f;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
 };
 int qmm_run_job(aex_ctx* ctx, const QmmJob& j, cudaStream_t s);
 int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s);

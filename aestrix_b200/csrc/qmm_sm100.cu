@@ -291,6 +291,19 @@ struct PairProblem {
   int glu_tile0;
   uint16_t* y2;
   int64_t ldy2;
+  // Weight tiles nt < qk_tiles hold the Q then K projections (128 columns per
+  // head, two heads per tile): their epilogue applies the joint attention's
+  // QK-RMSNorm + RoPE and writes head-major prep[which][head][tok0 + row][128]
+  // (which 0 = Q, 1 = K; heads h_total, tokens j_total), the layout the
+  // attention kernel reads, instead of y.
+  int qk_tiles;
+  uint16_t* prep;
+  int tok0, j_total, h_total;
+  const float* norm_q;  // [128] f32 (NULL: no norm)
+  const float* norm_k;
+  float eps;
+  const float* rope_cos;  // [j_total, 64] f32 (NULL: no rotation)
+  const float* rope_sin;
 };
 
 struct PairParams {
@@ -513,7 +526,77 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tc_fence_after();
       const int row = tl.mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 256;
-      if (tl.nt >= q.glu_tile0) {
+      if (tl.nt < q.qk_tiles) {
+        // QK-RMSNorm + RoPE of two heads (the reference's storage points: the linear's output rounded to bf16,
+        // f32 norm and rotation, one rounding; as qk_prep_kernel and AttentionUtils.processQKV / applyRopeBSHD).
+        const int heads_per_op = q.h_total;
+        const int tok = q.tok0 + row;
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int gh = tl.nt * 2 + h2;  // head index over Q then K
+          const int which = gh >= heads_per_op ? 1 : 0;
+          const int head = gh - which * heads_per_op;
+          const float* w = which ? q.norm_k : q.norm_q;
+          const uint32_t tb = tbase + h2 * 128;
+          // pass 1: sum of squares of the bf16-rounded outputs (pairs)
+          float2 ss2 = make_float2(0.f, 0.f);
+#pragma unroll 1
+          for (int c0 = 0; c0 < 128; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tb + c0, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const uint32_t hb = pack_bf16x2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+              const float2 v = make_float2(bf16lo_to_f32(hb), bf16hi_to_f32(hb));
+              ss2 = ffma2(v, v, ss2);
+            }
+          }
+          const float inv = rsqrtf((ss2.x + ss2.y) * (1.0f / 128.0f) + q.eps);
+          uint16_t* dst = q.prep + ((static_cast<int64_t>(which) * heads_per_op + head) * q.j_total + tok) * 128;
+          const float* crow = q.rope_cos ? q.rope_cos + static_cast<int64_t>(tok) * 64 : nullptr;
+          const float* srow = q.rope_sin ? q.rope_sin + static_cast<int64_t>(tok) * 64 : nullptr;
+          // pass 2: normalize, rotate, round once
+#pragma unroll 1
+          for (int c0 = 0; c0 < 128; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tb + c0, r);
+            tmem_wait_ld();
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float4 w0 = make_float4(inv, inv, inv, inv), w1 = w0;
+              if (w) {
+                w0 = __ldg(reinterpret_cast<const float4*>(w + c0 + i));
+                w1 = __ldg(reinterpret_cast<const float4*>(w + c0 + i + 4));
+                w0 = make_float4(w0.x * inv, w0.y * inv, w0.z * inv, w0.w * inv);
+                w1 = make_float4(w1.x * inv, w1.y * inv, w1.z * inv, w1.w * inv);
+              }
+              const float wl[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+              float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (crow) {
+                c4 = __ldg(reinterpret_cast<const float4*>(crow + (c0 + i) / 2));
+                s4 = __ldg(reinterpret_cast<const float4*>(srow + (c0 + i) / 2));
+              }
+              const float ca[4] = {c4.x, c4.y, c4.z, c4.w}, sa[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t hb = pack_bf16x2(__uint_as_float(r[i + 2 * e]), __uint_as_float(r[i + 2 * e + 1]));
+                // x * (w * inv): the prep kernel's x * inv * w up to the order of the product
+                const float2 x = fmul2(make_float2(bf16lo_to_f32(hb), bf16hi_to_f32(hb)),
+                                       make_float2(wl[2 * e], wl[2 * e + 1]));
+                const float re = x.x, im = x.y;
+                pk[(i >> 1) + e] = pack_bf16x2(re * ca[e] - im * sa[e], im * ca[e] + re * sa[e]);
+              }
+            }
+            if (row < q.m) {
+#pragma unroll
+              for (int i = 0; i < 16; i += 4)
+                *reinterpret_cast<uint4*>(dst + c0 + 2 * i) = make_uint4(pk[i], pk[i + 1], pk[i + 2], pk[i + 3]);
+            }
+          }
+        }
+      } else if (tl.nt >= q.glu_tile0) {
         // Gate columns [0, 128), up columns [128, 256) of this tile.
         uint16_t* yr = q.y2 + static_cast<int64_t>(row) * q.ldy2 + (tl.nt - q.glu_tile0) * 128;
 #pragma unroll 1
@@ -904,6 +987,16 @@ int launch_gemm_pair(aex_ctx* ctx, const QmmJob* jobs, int n_jobs, cudaStream_t 
     q.glu_tile0 = j.glu_tile0;
     q.y2 = j.y2;
     q.ldy2 = j.ldy2;
+    q.qk_tiles = j.qk_tiles;
+    q.prep = j.prep;
+    q.tok0 = j.tok0;
+    q.j_total = j.j_total;
+    q.h_total = j.h_total;
+    q.norm_q = j.norm_q;
+    q.norm_k = j.norm_k;
+    q.eps = j.eps;
+    q.rope_cos = j.rope_cos;
+    q.rope_sin = j.rope_sin;
     tiles += q.m_tiles * j.w->n_tiles;
   }
   if (n_jobs == 1) tm[1] = tm[0];
@@ -938,7 +1031,7 @@ int launch_gemm_pair(aex_ctx* ctx, const QmmJob* jobs, int n_jobs, cudaStream_t 
 
 bool gemv_path(const aex_qweight* w, int m) { return m <= 16 && w->k_blocks <= qmm::kGemvMaxSplit * qmm::kGemvMaxKbps; }
 // The GEMV has no SwiGLU epilogue: jobs that need it take the GEMM at any m.
-bool use_gemv(const QmmJob& j) { return gemv_path(j.w, j.m) && j.glu_tile0 >= j.w->n_tiles; }
+bool use_gemv(const QmmJob& j) { return gemv_path(j.w, j.m) && j.glu_tile0 >= j.w->n_tiles && j.qk_tiles == 0; }
 
 int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
   const aex_qweight* w = j.w;
@@ -959,6 +1052,9 @@ int check_job(aex_ctx* ctx, const QmmJob& j) {
   if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
   if (j.glu_tile0 < j.w->n_tiles && (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8))
     return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows");
+  if (j.qk_tiles > 0 && (!j.prep || (reinterpret_cast<uintptr_t>(j.prep) & 15) || j.qk_tiles != j.h_total ||
+                         j.tok0 < 0 || j.tok0 + j.m > j.j_total))
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "qk prep epilogue: bad destination, head or token range");
   return AEX_OK;
 }
 
