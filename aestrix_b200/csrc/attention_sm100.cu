@@ -460,7 +460,9 @@ struct PrepParams {
   const float* sin_t;
   float eps;
   int batch, seq, heads;
-  __nv_bfloat16* out;  // [2][B][H][S][128]
+  __nv_bfloat16* out;    // Q (and K when k_out is NULL): [2][B][H][S][128]
+  __nv_bfloat16* k_out;  // K elsewhere: [B][H][S][128], or [B][S][H][128] when k_token_major
+  int k_token_major;
 };
 
 // Each half-warp owns one 128-wide row (16 lanes x 8 elements = one 16-byte
@@ -567,10 +569,16 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
       }
     }
     if (valid) {
-      const int64_t dst = static_cast<int64_t>(c.which) * rows_per_op * kD +
-                          (static_cast<int64_t>(c.b * heads + c.h) * seq + c.s) * kD + l16 * 8;
-      *reinterpret_cast<uint4*>(p.out + dst) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
-                                                          pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+      __nv_bfloat16* base = p.out;
+      int64_t dst = static_cast<int64_t>(c.which) * rows_per_op * kD +
+                    (static_cast<int64_t>(c.b * heads + c.h) * seq + c.s) * kD;
+      if (c.which && p.k_out) {
+        base = p.k_out;
+        dst = p.k_token_major ? (static_cast<int64_t>(c.b * seq + c.s) * heads + c.h) * kD
+                              : (static_cast<int64_t>(c.b * heads + c.h) * seq + c.s) * kD;
+      }
+      *reinterpret_cast<uint4*>(base + dst + l16 * 8) = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                                                                  pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
     }
     c.advance(2, heads, seq, batch);
   }
@@ -629,7 +637,8 @@ int bshd_tmap(aex_ctx* ctx, CUtensorMap* m, const void* base, int64_t sb, int64_
 
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
                    int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
-                   float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream) {
+                   float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream, void* k_out,
+                   bool k_token_major) {
   if (B <= 0 || S <= 0 || H <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "qk prep: empty batch, seq or heads");
   attn::PrepParams pp{};
   pp.q = static_cast<const __nv_bfloat16*>(q);
@@ -652,6 +661,8 @@ int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void*
   pp.seq = S;
   pp.heads = H;
   pp.out = static_cast<__nv_bfloat16*>(out);
+  pp.k_out = static_cast<__nv_bfloat16*>(k_out);
+  pp.k_token_major = k_token_major ? 1 : 0;
   const int64_t rows = 2ll * B * S * H;
   const int64_t per_block = attn::kPrepWarps * attn::kPrepRowsPerWarp;
   const int64_t blocks = (rows + per_block - 1) / per_block;

@@ -215,22 +215,25 @@ int ln_mod_rows(aex_dit* d, const float* x, int rows, const float* scale, const 
   return glue::ln_mod(d->ctx, x, d->C, rows, d->C, scale, shift, d->cfg.ln_eps, y, d->C, s);
 }
 
-// Where the Q|K projections go after QK-RMSNorm + RoPE (the QKV GEMM's
-// epilogue writes them): head-major [2][H][J][128], this GPU's PREP buffer or,
-// sequence-parallel, the local Q / K ring slot 0 of the ring state.
-int qk_destination(aex_dit* d, uint16_t** dst) {
-  if (d->comm) {
-    uint16_t *K0 = nullptr, *V0 = nullptr;
-    return ring_buffers(d->ctx, d->comm, d->J, d->H, dst, &K0, &V0);
-  }
-  *dst = d->PREP;
+// Where Q, K and V go for the joint attention: Q and K after QK-RMSNorm + RoPE
+// (the QKV GEMM's epilogue writes them) head-major [2][H][J][128] in this GPU's
+// PREP buffer or, sequence-parallel, this rank's slots of the exchange state
+// (V then copied into its slot by joint_attend).
+int qk_destination(aex_dit* d, SpSlots* sl) {
+  if (d->comm) return sp_buffers(d->ctx, d->comm, d->J, d->H, sl);
+  sl->q = d->PREP;
+  sl->k = nullptr;
+  sl->k_token_major = false;
+  sl->v = nullptr;
   return AEX_OK;
 }
 
 // A QKV job with the QK-RMSNorm + RoPE epilogue for rows [tok0, tok0 + m) of the joint sequence.
-void with_qk_prep(aex_dit* d, QmmJob& j, uint16_t* prep, int tok0, const float* wq, const float* wk) {
+void with_qk_prep(aex_dit* d, QmmJob& j, const SpSlots& sl, int tok0, const float* wq, const float* wk) {
   j.qk_tiles = d->H;
-  j.prep = prep;
+  j.prep = sl.q;
+  j.prep_k = sl.k;
+  j.k_tok_major = sl.k_token_major;
   j.tok0 = tok0;
   j.j_total = d->J;
   j.h_total = d->H;
@@ -242,16 +245,14 @@ void with_qk_prep(aex_dit* d, QmmJob& j, uint16_t* prep, int tok0, const float* 
 }
 
 // Joint attention on the prepared Q / K (qk_destination) and the V columns of PROJ (row pitch ld) into out:
-// on this GPU, or as a ring over the sequence shards of all ranks.
-int joint_attend(aex_dit* d, int64_t ld, uint16_t* out, int64_t out_ld, cudaStream_t s) {
+// on this GPU, or over the sequence shards of all ranks.
+int joint_attend(aex_dit* d, const SpSlots& sl, int64_t ld, uint16_t* out, int64_t out_ld, cudaStream_t s) {
   const int J = d->J, H = d->H, C = d->C;
   const uint16_t* v = d->PROJ + 2 * C;
   if (d->comm) {
-    uint16_t *Q = nullptr, *K0 = nullptr, *V0 = nullptr;
-    AEX_TRY(ring_buffers(d->ctx, d->comm, J, H, &Q, &K0, &V0));
-    AEX_CUDA_TRY(d->ctx, cudaMemcpy2DAsync(V0, static_cast<size_t>(H) * 256, v, static_cast<size_t>(ld) * 2,
+    AEX_CUDA_TRY(d->ctx, cudaMemcpy2DAsync(sl.v, static_cast<size_t>(H) * 256, v, static_cast<size_t>(ld) * 2,
                                            static_cast<size_t>(H) * 256, J, cudaMemcpyDeviceToDevice, s));
-    return ring_run(d->ctx, d->comm, J, H, 1.0f / std::sqrt(128.0f), out, out_ld, 128, s);
+    return sp_run(d->ctx, d->comm, J, H, 1.0f / std::sqrt(128.0f), out, out_ld, 128, s);
   }
   return attend(d, v, ld, out, out_ld, s);
 }
@@ -283,14 +284,14 @@ int double_block(aex_dit* d, int i, cudaStream_t s) {
   const int64_t pq = 3 * C;  // PROJ row pitch for Q|K|V
   // Each text-stream linear shares one launch with its image-stream twin. Q and K leave the GEMM normalized
   // and rotated (per-stream norm weights: norm_added_* on text rows, norm_* on image rows); V goes to PROJ.
-  uint16_t* prep = nullptr;
-  AEX_TRY(qk_destination(d, &prep));
+  SpSlots sl{};
+  AEX_TRY(qk_destination(d, &sl));
   QmmJob jt{qkv_t, NHt, C, lt, d->PROJ, pq, 0, nullptr};
   QmmJob ji{qkv_i, NHi, C, li, d->PROJ + static_cast<int64_t>(lt) * pq, pq, 0, nullptr};
-  with_qk_prep(d, jt, prep, 0, naq, nak);
-  with_qk_prep(d, ji, prep, lt, nq, nk);
+  with_qk_prep(d, jt, sl, 0, naq, nak);
+  with_qk_prep(d, ji, sl, lt, nq, nk);
   AEX_TRY(run_jobs(d, jt, ji, s));
-  AEX_TRY(joint_attend(d, pq, d->ATT, C, s));
+  AEX_TRY(joint_attend(d, sl, pq, d->ATT, C, s));
   AEX_TRY(run_jobs(d, QmmJob{out_t, d->ATT, C, lt, Xt, C, 2, mt + 2 * C},
                    QmmJob{out_i, d->ATT + static_cast<int64_t>(lt) * C, C, li, Xi, C, 2, mi + 2 * C}, s));
   // MLP half (per stream)
@@ -326,11 +327,11 @@ int single_block(aex_dit* d, int i, cudaStream_t s) {
   pj.glu_tile0 = 3 * C / 256;
   pj.y2 = d->ATT + C;
   pj.ldy2 = d->cat;
-  uint16_t* prep = nullptr;
-  AEX_TRY(qk_destination(d, &prep));
-  with_qk_prep(d, pj, prep, 0, nq, nk);  // Q, K normalized and rotated in the epilogue
+  SpSlots sl{};
+  AEX_TRY(qk_destination(d, &sl));
+  with_qk_prep(d, pj, sl, 0, nq, nk);  // Q, K normalized and rotated in the epilogue
   AEX_TRY(qmm_run_job(d->ctx, pj, s));
-  AEX_TRY(joint_attend(d, pp, d->ATT, d->cat, s));
+  AEX_TRY(joint_attend(d, sl, pp, d->ATT, d->cat, s));
   AEX_TRY(qmm_run(d->ctx, out, d->ATT, d->cat, J, d->X, C, 2, ms + 2 * C, s));
   return AEX_OK;
 }

@@ -87,6 +87,10 @@ struct QmmJob {
   // this job being token tok0 + r.
   int qk_tiles = 0;
   uint16_t* prep = nullptr;
+  // K elsewhere (NULL: in prep after Q): [h_total][j_total][128], or
+  // token-major [j_total][h_total][128] when k_tok_major.
+  uint16_t* prep_k = nullptr;
+  bool k_tok_major = false;
   int tok0 = 0, j_total = 0, h_total = 0;
   const float* norm_q = nullptr;
   const float* norm_k = nullptr;
@@ -105,25 +109,33 @@ int qmm_glu_interleave(aex_ctx* ctx, const aex_qweight* src, int plain_rows, int
 // s < split use (wq_a, wk_a), the others (wq, wk).
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
                    int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
-                   float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream);
+                   float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream,
+                   void* k_out = nullptr, bool k_token_major = false);
 // The attention kernel on prepared operands: strided [B, S, H, 128] views
 // (strides in elements: batch, seq, head) for Q/O with S rows and K/V with
 // S_kv rows; optional per-row log2-sum-exp output lse[b*lse_sb + h*lse_sh + row].
 int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
                           const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
                           float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream);
-// Ring attention internals (ring_attention.cpp) for callers that prepare Q/K
-// themselves: the local Q plane and K ring slot 0 (head-major [H][S][128],
-// adjacent, as written by launch_qk_prep) and V ring slot 0 (token-major
-// [S][H*128]) of this communicator's ring state, grown to S rows of H heads;
-// then the hop loop over all ranks (joint attention of the local queries
-// against every rank's K/V, merged by log-sum-exp) into out (bf16, strides
-// in elements: token, head).
-int ring_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, uint16_t** q, uint16_t** k0, uint16_t** v0);
+// Sequence-parallel attention internals (ring_attention.cpp) for callers that
+// prepare Q/K themselves. sp_buffers grows this communicator's state for S
+// local rows of H heads and returns where the local operands go: Q head-major
+// [H][S][128]; K head-major (directly after Q) or token-major [S][H][128]
+// (k_token_major); V token-major [S][H][128]. sp_run then computes the joint
+// attention of the local queries against every rank's K/V into out (bf16,
+// strides in elements: token, head), by the schedule sp_buffers chose (a ring
+// of NCCL sends with log-sum-exp merges, or one all-gather and one call).
+struct SpSlots {
+  uint16_t* q;
+  uint16_t* k;
+  bool k_token_major;
+  uint16_t* v;
+};
+int sp_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, SpSlots* out);
 int comm_world(const aex_comm* c);
 int comm_rank(const aex_comm* c);
-int ring_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
-             cudaStream_t s);
+int sp_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
+           cudaStream_t s);
 // The context a DiT engine was created on.
 aex_ctx* dit_context(aex_dit* d);
 // Attention (and prep if args ask for it) on validated args.

@@ -295,9 +295,12 @@ struct PairProblem {
   // head, two heads per tile): their epilogue applies the joint attention's
   // QK-RMSNorm + RoPE and writes head-major prep[which][head][tok0 + row][128]
   // (which 0 = Q, 1 = K; heads h_total, tokens j_total), the layout the
-  // attention kernel reads, instead of y.
+  // attention kernel reads, instead of y. K goes to prep_k instead when it is
+  // set: [h_total][j_total][128], or [j_total][h_total][128] when k_tok_major.
   int qk_tiles;
   uint16_t* prep;
+  uint16_t* prep_k;
+  int k_tok_major;
   int tok0, j_total, h_total;
   const float* norm_q;  // [128] f32 (NULL: no norm)
   const float* norm_k;
@@ -554,6 +557,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           const float inv = rsqrtf((ss2.x + ss2.y) * (1.0f / 128.0f) + q.eps);
           uint16_t* dst = q.prep + ((static_cast<int64_t>(which) * heads_per_op + head) * q.j_total + tok) * 128;
+          if (which && q.prep_k)
+            dst = q.prep_k + (q.k_tok_major ? static_cast<int64_t>(tok) * heads_per_op + head
+                                            : static_cast<int64_t>(head) * q.j_total + tok) * 128;
           const float* crow = q.rope_cos ? q.rope_cos + static_cast<int64_t>(tok) * 64 : nullptr;
           const float* srow = q.rope_sin ? q.rope_sin + static_cast<int64_t>(tok) * 64 : nullptr;
           // pass 2: normalize, rotate, round once
@@ -989,6 +995,8 @@ int launch_gemm_pair(aex_ctx* ctx, const QmmJob* jobs, int n_jobs, cudaStream_t 
     q.ldy2 = j.ldy2;
     q.qk_tiles = j.qk_tiles;
     q.prep = j.prep;
+    q.prep_k = j.prep_k;
+    q.k_tok_major = j.k_tok_major ? 1 : 0;
     q.tok0 = j.tok0;
     q.j_total = j.j_total;
     q.h_total = j.h_total;
@@ -1052,7 +1060,8 @@ int check_job(aex_ctx* ctx, const QmmJob& j) {
   if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
   if (j.glu_tile0 < j.w->n_tiles && (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8))
     return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows");
-  if (j.qk_tiles > 0 && (!j.prep || (reinterpret_cast<uintptr_t>(j.prep) & 15) || j.qk_tiles != j.h_total ||
+  if (j.qk_tiles > 0 && (!j.prep || (reinterpret_cast<uintptr_t>(j.prep) & 15) ||
+                         (reinterpret_cast<uintptr_t>(j.prep_k) & 15) || j.qk_tiles != j.h_total ||
                          j.tok0 < 0 || j.tok0 + j.m > j.j_total))
     return set_error(ctx, AEX_ERR_INVALID_ARG, "qk prep epilogue: bad destination, head or token range");
   return AEX_OK;

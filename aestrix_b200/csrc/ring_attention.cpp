@@ -7,11 +7,13 @@
 // sequence is split into P equal contiguous shards (rank r holds tokens
 // [r*S_r, (r+1)*S_r), text rows in shard 0). Each rank RMS-normalizes and
 // rotates its own Q and K rows (RoPE uses absolute positions, so rotating
-// before the exchange is exact), then for hop h = 0..P-1 attends its queries to
-// the K/V shard of rank (r - h) mod P while the next shard travels around the
-// ring (ncclSend to r+1 / ncclRecv from r-1 on a dedicated stream, double
-// buffered). Partial outputs are merged by their log-sum-exp
-// (ring_kernels.cu).
+// before the exchange is exact). Two schedules, the same on every rank:
+//  * ring: for hop h = 0..P-1 attend the local queries to the K/V shard of rank
+//    (r - h) mod P while the next shard travels around the ring (ncclSend to
+//    r+1 / ncclRecv from r-1 on a dedicated stream, double buffered); partial
+//    outputs merged by their log-sum-exp (ring_kernels.cu);
+//  * gather: one ncclAllGather of every rank's K and V (token-major, in place)
+//    and one attention call of the local queries over all P*S keys.
 //
 // NCCL is resolved at run time (the copy already loaded in the process, else
 // libnccl.so.2), so the library has no link-time NCCL dependency.
@@ -19,6 +21,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <thread>
@@ -42,6 +45,7 @@ struct NcclApi {
   decltype(&ncclCommGetAsyncError) commGetAsyncError = nullptr;
   decltype(&ncclSend) send = nullptr;
   decltype(&ncclRecv) recv = nullptr;
+  decltype(&ncclAllGather) allGather = nullptr;
   decltype(&ncclGroupStart) groupStart = nullptr;
   decltype(&ncclGroupEnd) groupEnd = nullptr;
   decltype(&ncclGetErrorString) errorString = nullptr;
@@ -63,17 +67,54 @@ const NcclApi& nccl() {
     sym(api.commGetAsyncError, "ncclCommGetAsyncError");
     sym(api.send, "ncclSend");
     sym(api.recv, "ncclRecv");
+    sym(api.allGather, "ncclAllGather");
     sym(api.groupStart, "ncclGroupStart");
     sym(api.groupEnd, "ncclGroupEnd");
     sym(api.errorString, "ncclGetErrorString");
     api.ok = api.getUniqueId && api.commInitRankConfig && api.commDestroy && api.commAbort && api.commGetAsyncError &&
-             api.send && api.recv && api.groupStart && api.groupEnd && api.errorString;
+             api.send && api.recv && api.allGather && api.groupStart && api.groupEnd && api.errorString;
   });
   return api;
 }
 
 int nccl_error(aex_ctx* ctx, ncclResult_t r, const char* what) {
   return set_error(ctx, AEX_ERR_NCCL, "%s failed: %s", what, nccl().errorString ? nccl().errorString(r) : "?");
+}
+
+// ncclGroupEnd on a non-blocking communicator: wait (bounded) until the group
+// is enqueued on its stream.
+int group_end(aex_ctx* ctx, ncclComm_t comm, ncclResult_t issued, const char* what) {
+  ncclResult_t ne = nccl().groupEnd();
+  if (issued != ncclSuccess && issued != ncclInProgress) return nccl_error(ctx, issued, what);
+  const auto t0 = std::chrono::steady_clock::now();
+  while (ne == ncclInProgress) {
+    ncclResult_t st = ncclInProgress;
+    const ncclResult_t q = nccl().commGetAsyncError(comm, &st);
+    if (q != ncclSuccess) return nccl_error(ctx, q, "ncclCommGetAsyncError");
+    ne = st;
+    if (ne == ncclInProgress && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30))
+      return set_error(ctx, AEX_ERR_TIMEOUT, "NCCL group not enqueued after 30 s");
+  }
+  if (ne != ncclSuccess) return nccl_error(ctx, ne, "ncclGroupEnd");
+  return AEX_OK;
+}
+
+// Schedule of the sequence-parallel attention, the same on every rank (it
+// depends only on the shapes, equal on all ranks): one all-gather of K/V and
+// one attention call over all keys measured faster than the ring at every P
+// tried (2048^2, P = 2: 1.74 vs 1.81 ms per call), so it is the default while
+// the gathered K and V fit in kGatherMaxBytes; longer sequences take the ring,
+// whose memory per rank stays O(S). AEX_SP_SCHEDULE=ring or =gather overrides.
+constexpr size_t kGatherMaxBytes = size_t{8} << 30;
+
+bool use_gather(int P, size_t plane_bytes) {
+  static const int forced = [] {
+    const char* e = getenv("AEX_SP_SCHEDULE");
+    if (!e) return -1;
+    return !strcmp(e, "gather") ? 1 : !strcmp(e, "ring") ? 0 : -1;
+  }();
+  if (forced >= 0) return forced == 1;
+  return 2 * static_cast<size_t>(P) * plane_bytes <= kGatherMaxBytes;
 }
 
 }  // namespace
@@ -116,23 +157,39 @@ namespace aex {
 int comm_world(const aex_comm* c) { return c->world; }
 int comm_rank(const aex_comm* c) { return c->rank; }
 
-int ring_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, uint16_t** q, uint16_t** k0, uint16_t** v0) {
+// Ring layout: Q plane | K ring[2] (head-major) | V ring[2] (token-major) | O_h bf16 | O_acc f32 | lse_h |
+// lse ping-pong[2] (Q and K ring[0] adjacent: one prep writes both).
+// Gather layout: Q plane (head-major) | K all ranks [P*S][H][128] | V all ranks [P*S][H][128] (token-major;
+// this rank's rows at r*S).
+int sp_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, SpSlots* out) {
   if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
+  const int P = c->world, r = c->rank;
   const size_t plane = static_cast<size_t>(H) * S * 128;
-  // Layout of the ring state: Q plane | K ring[2] (head-major) | V ring[2] (token-major) |
-  // O_h bf16 | O_acc f32 | lse_h | lse ping-pong[2]. Q and K ring[0] are adjacent (one prep writes both).
-  const size_t bq = align256(plane * 2), bkv = align256(plane * 2), bo = align256(plane * 2),
-               bacc = align256(plane * 4), blse = align256(static_cast<size_t>(H) * S * 4);
-  if (bq != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
+  if (align256(plane * 2) != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
+  uint8_t* base;
+  if (use_gather(P, plane * 2)) {
+    if (int e = grow(c, plane * 2 * (1 + 2 * static_cast<size_t>(P)))) return e;
+    base = static_cast<uint8_t*>(c->buf);
+    out->q = reinterpret_cast<uint16_t*>(base);
+    out->k = reinterpret_cast<uint16_t*>(base + plane * 2) + r * plane;
+    out->k_token_major = true;
+    out->v = reinterpret_cast<uint16_t*>(base + plane * 2 * (1 + static_cast<size_t>(P))) + r * plane;
+    return AEX_OK;
+  }
+  const size_t bq = plane * 2, bkv = plane * 2, bo = plane * 2, bacc = plane * 4,
+               blse = align256(static_cast<size_t>(H) * S * 4);
   const size_t off_k = bq, off_v = off_k + 2 * bkv, off_o = off_v + 2 * bkv, off_acc = off_o + bo,
                off_lh = off_acc + bacc, off_l0 = off_lh + blse, total = off_l0 + 2 * blse;
   if (int e = grow(c, total)) return e;
-  uint8_t* base = static_cast<uint8_t*>(c->buf);
-  *q = reinterpret_cast<uint16_t*>(base);
-  *k0 = reinterpret_cast<uint16_t*>(base + off_k);
-  *v0 = reinterpret_cast<uint16_t*>(base + off_v);
+  base = static_cast<uint8_t*>(c->buf);
+  out->q = reinterpret_cast<uint16_t*>(base);
+  out->k = reinterpret_cast<uint16_t*>(base + off_k);
+  out->k_token_major = false;
+  out->v = reinterpret_cast<uint16_t*>(base + off_v);
   return AEX_OK;
 }
+
+namespace {
 
 int ring_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
              cudaStream_t s) {
@@ -167,19 +224,7 @@ int ring_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, in
       if (nr == ncclSuccess) nr = nccl().send(Vr[cur], kv_bytes, ncclChar, next, c->comm, c->stream);
       if (nr == ncclSuccess) nr = nccl().recv(Kr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
       if (nr == ncclSuccess) nr = nccl().recv(Vr[nxt], kv_bytes, ncclChar, prev, c->comm, c->stream);
-      ncclResult_t ne = nccl().groupEnd();
-      if (nr != ncclSuccess && nr != ncclInProgress) return nccl_error(ctx, nr, "ncclSend/ncclRecv");
-      // Non-blocking communicator: wait (bounded) until the group is enqueued on the stream.
-      const auto t0 = std::chrono::steady_clock::now();
-      while (ne == ncclInProgress) {
-        ncclResult_t st = ncclInProgress;
-        const ncclResult_t q = nccl().commGetAsyncError(c->comm, &st);
-        if (q != ncclSuccess) return nccl_error(ctx, q, "ncclCommGetAsyncError");
-        ne = st;
-        if (ne == ncclInProgress && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30))
-          return set_error(ctx, AEX_ERR_TIMEOUT, "NCCL group not enqueued after 30 s");
-      }
-      if (ne != ncclSuccess) return nccl_error(ctx, ne, "ncclGroupEnd");
+      if (int e = group_end(ctx, c->comm, nr, "ncclSend/ncclRecv")) return e;
       AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_recv, c->stream));
     }
     // Attention of the local queries against the shard in hand, then merge.
@@ -193,6 +238,47 @@ int ring_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, in
     if (hop + 1 < P) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(s, c->ev_recv, 0));
   }
   return AEX_OK;
+}
+
+
+// K/V of every rank gathered in place (one grouped ncclAllGather on the exchange stream), then one attention
+// call of the local queries over all P*S keys.
+int gather_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
+               cudaStream_t s) {
+  const int P = c->world;
+  const size_t plane = static_cast<size_t>(H) * S * 128;
+  uint8_t* base = static_cast<uint8_t*>(c->buf);
+  uint16_t* Q = reinterpret_cast<uint16_t*>(base);
+  uint16_t* Kall = reinterpret_cast<uint16_t*>(base + plane * 2);
+  uint16_t* Vall = reinterpret_cast<uint16_t*>(base + plane * 2 * (1 + static_cast<size_t>(P)));
+  AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_start, s));
+  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_start, 0));
+  const size_t bytes = plane * 2;
+  ncclResult_t nr = nccl().groupStart();
+  if (nr == ncclSuccess)
+    nr = nccl().allGather(reinterpret_cast<uint8_t*>(Kall) + c->rank * bytes, Kall, bytes, ncclChar, c->comm,
+                          c->stream);
+  if (nr == ncclSuccess)
+    nr = nccl().allGather(reinterpret_cast<uint8_t*>(Vall) + c->rank * bytes, Vall, bytes, ncclChar, c->comm,
+                          c->stream);
+  if (int e = group_end(ctx, c->comm, nr, "ncclAllGather")) return e;
+  AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_recv, c->stream));
+  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(s, c->ev_recv, 0));
+  const int64_t q_st[3] = {static_cast<int64_t>(plane), 128, static_cast<int64_t>(S) * 128};  // head-major
+  const int64_t kv_st[3] = {static_cast<int64_t>(P) * static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128,
+                            128};  // token-major over all ranks
+  const int64_t o_st[3] = {static_cast<int64_t>(S) * out_ss, out_ss, out_sh};
+  return launch_attention_core(ctx, Q, q_st, Kall, kv_st, Vall, kv_st, out, o_st, 1, S, P * S, H, scale, nullptr, 0,
+                               0, s);
+}
+
+}  // namespace
+
+int sp_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
+           cudaStream_t s) {
+  if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
+  return use_gather(c->world, static_cast<size_t>(H) * S * 256) ? gather_run(ctx, c, S, H, scale, out, out_ss, out_sh, s)
+                              : ring_run(ctx, c, S, H, scale, out, out_ss, out_sh, s);
 }
 
 }  // namespace aex
@@ -278,6 +364,11 @@ int aex_comm_abort(aex_comm* c) {
   return r == ncclSuccess ? AEX_OK : AEX_ERR_NCCL;
 }
 
+int aex_sp_schedule(int world, int seq, int heads) {
+  if (world < 1 || seq <= 0 || heads <= 0) return -1;
+  return aex::use_gather(world, static_cast<size_t>(heads) * seq * 256) ? 1 : 0;
+}
+
 int aex_ring_attention(aex_ctx* ctx, aex_comm* c, const aex_attention_args* a, aex_stream stream) {
   using namespace aex;
   if (!ctx || !c || !a) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL argument");
@@ -289,20 +380,19 @@ int aex_ring_attention(aex_ctx* ctx, aex_comm* c, const aex_attention_args* a, a
   if (int r = bind_device(ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
   const int S = a->seq, H = a->heads;
-  uint16_t *Q = nullptr, *K0 = nullptr, *V0 = nullptr;
-  if (int e = ring_buffers(ctx, c, S, H, &Q, &K0, &V0)) return e;
-  // 1. This rank's Q and K: norm + RoPE (rows of the local shard) straight into Q and K ring[0]
-  //    (the prep writes the Q plane, then the K plane, contiguously; K ring[0] follows Q).
+  SpSlots sl{};
+  if (int e = sp_buffers(ctx, c, S, H, &sl)) return e;
+  // 1. This rank's Q and K: norm + RoPE (rows of the local shard, absolute positions) into their slots.
   const int64_t qs[3] = {a->q.stride_b, a->q.stride_s, a->q.stride_h};
   const int64_t ks[3] = {a->k.stride_b, a->k.stride_s, a->k.stride_h};
   if (int e = launch_qk_prep(ctx, a->q.data, qs, a->k.data, ks, 1, S, H, a->norm_q_weight, a->norm_k_weight, nullptr,
-                             nullptr, 0, a->eps, a->rope_cos, a->rope_sin, Q, s))
+                             nullptr, 0, a->eps, a->rope_cos, a->rope_sin, sl.q, s, sl.k, sl.k_token_major))
     return e;
-  // 2. This rank's V into V ring[0] (token-major, contiguous rows of H*128).
-  AEX_CUDA_TRY(ctx, cudaMemcpy2DAsync(V0, static_cast<size_t>(H) * 256, a->v.data,
+  // 2. This rank's V into its slot (token-major, contiguous rows of H*128).
+  AEX_CUDA_TRY(ctx, cudaMemcpy2DAsync(sl.v, static_cast<size_t>(H) * 256, a->v.data,
                                       static_cast<size_t>(a->v.stride_s) * 2, static_cast<size_t>(H) * 256, S,
                                       cudaMemcpyDeviceToDevice, s));
-  return ring_run(ctx, c, S, H, a->scale, a->out.data, a->out.stride_s, a->out.stride_h, s);
+  return sp_run(ctx, c, S, H, a->scale, a->out.data, a->out.stride_s, a->out.stride_h, s);
 }
 
 }  // extern "C"

@@ -367,7 +367,8 @@ def measure_dit(ctx, dev, world, runs=3):
     fl = dit.dit_flops(cfg)
     ok = bool(torch.isfinite(lat).all().item())
     eng.close()
-    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "images_per_s": world * 4000.0 / ms / 4,
+    schedule = {0: "ring", 1: "all-gather"}.get(_lib.lib().aex_sp_schedule(world, Jp, full.heads), "?")
+    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "schedule": schedule, "images_per_s": world * 4000.0 / ms / 4,
             "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12, "tflop_per_step": fl["total"] / 1e12,
             "flops_split_per_step": {"linear": fl["linear"] / 1e12, "attention": fl["attention"] / 1e12},
             "n_gpus": world, "batch": world, "finite": ok,
@@ -396,9 +397,9 @@ def _make_comm(ctx, dev, world, rank):
 
 
 def measure_dit_sp(ctx, dev, world, rank, runs=2):
-    """SURVEY config 5 at the DiT level: the 4-step FLUX.2-klein denoise of ONE 2048^2 image (512 text +
+    """The long-sequence configuration at the DiT level: the 4-step FLUX.2-klein denoise of ONE 2048^2 image (512 text +
     128x128 image tokens, J = 16,896) sequence-parallel over the N GPUs (aex_dit_set_sequence_parallel:
-    contiguous shards of J/N tokens, text on rank 0, each block's joint attention as a ring over NCCL).
+    contiguous shards of J/N tokens, text on rank 0, each block's joint attention over NCCL per aex_sp_schedule).
     Random-init 4-bit weights as configs[3]. Device time of aex_dit_denoise, max over ranks; TFLOP/s
     counts the whole image's linears and attention."""
     import torch
@@ -450,14 +451,15 @@ def measure_dit_sp(ctx, dev, world, rank, runs=2):
     eng.close()
     _lib.lib().aex_comm_destroy(comm)
     fl = dit.dit_flops(full)
-    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12,
+    schedule = {0: "ring", 1: "all-gather"}.get(_lib.lib().aex_sp_schedule(world, Jp, full.heads), "?")
+    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "schedule": schedule, "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12,
             "tflop_per_step": fl["total"] / 1e12, "shard_tokens": Jp, "n_gpus": world, "finite": ok,
-            "config": "SURVEY config 5: FLUX.2-klein 2048^2 (J=16,896), 4 steps, one image sequence-parallel "
+            "config": "FLUX.2-klein 2048^2 (J=16,896), 4 steps, one image sequence-parallel "
                       "over the GPUs, random-init 4-bit weights"}
 
 
 def measure_i2i(ctx, dev, iters=40):
-    """SURVEY config 5 (i2i): joint attention over 512 text + 64x64 target + 64x64 reference tokens
+    """Image-to-image conditioning: joint attention over 512 text + 64x64 target + 64x64 reference tokens
     (J = 8,704, 24 x 128, bf16, fused QK-RMSNorm + RoPE; reference ids (10, h, w, 0)), one GPU.
     Two input sets (each > L2 with the outputs). TFLOP/s counts 4*S^2*D*H = 930.9 GFLOP per call."""
     import torch
@@ -493,14 +495,15 @@ def measure_i2i(ctx, dev, iters=40):
     ms = e0.elapsed_time(e1) / iters
     flops = 4.0 * S * S * HEAD_DIM * HEADS
     return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "gflop_per_call": flops / 1e9, "seq": S,
-            "config": "SURVEY config 5 i2i: 512 text + 4096 target + 4096 reference tokens, fused call"}
+            "config": "i2i: 512 text + 4096 target + 4096 reference tokens, fused call"}
 
 
 def measure_ring(ctx, dev, world, rank, iters=5):
     """joint attention at 2048^2 (512 text + 16384 image tokens = 16896, 24 x 128,
-    bf16, fused QK-RMSNorm + RoPE), sequence-parallel ring attention over the N GPUs (contiguous shards,
-    K/V exchanged with NCCL over NVLink and overlapped with compute). Device time, max over ranks;
-    TFLOP/s counts the whole call's 4*S^2*D*H."""
+    bf16, fused QK-RMSNorm + RoPE), sequence-parallel attention over the N GPUs (contiguous shards; K/V
+    exchanged with NCCL over NVLink: one all-gather then one attention call, or a ring of hops overlapped
+    with compute, per aex_sp_schedule). Device time, max over ranks; TFLOP/s counts the whole call's
+    4*S^2*D*H."""
     import ctypes as C
 
     import torch
@@ -537,10 +540,11 @@ def measure_ring(ctx, dev, world, rank, iters=5):
     ctx.sync(stream.cuda_stream)
     L.aex_comm_destroy(comm)
     flops = 4.0 * S * S * HEAD_DIM * H
-    kv_bytes_per_hop = 2 * Sp * H * HEAD_DIM * 2
+    kv_bytes_per_rank = 2 * Sp * H * HEAD_DIM * 2
+    schedule = {0: "ring", 1: "all-gather"}.get(L.aex_sp_schedule(world, Sp, H), "?")
     return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "gflop_per_call": flops / 1e9, "seq": S,
-            "shard": Sp, "hops": world, "kv_bytes_per_hop": kv_bytes_per_hop,
-            "config": "BASELINE configs[4]: 2048^2 joint attention, sequence-parallel ring over NCCL"}
+            "shard": Sp, "schedule": schedule, "kv_bytes_per_rank": kv_bytes_per_rank,
+            "config": "BASELINE configs[4]: 2048^2 joint attention, sequence-parallel over NCCL"}
 
 
 def run_ours(args):
@@ -690,7 +694,7 @@ def run_ours(args):
         if dit_res is not None:
             line["dit_denoise"] = dit_res
         if ring_res is not None:
-            line["ring_attention_2048"] = ring_res
+            line["sp_attention_2048"] = ring_res
         line["joint_attention_i2i"] = i2i_res
         if sp_res is not None:
             line["dit_denoise_2048_sequence_parallel"] = sp_res

@@ -281,7 +281,10 @@ int aex_safetensors_scan(const char* path, char* out, size_t out_len);
 
 /* ------------------------------------------------ multi-GPU (NCCL, NVLink) */
 
-/* Sequence-parallel ring attention over P GPUs, one process per GPU. No
+/* Sequence-parallel attention over P GPUs, one process per GPU: a ring of
+ * NCCL point-to-point K/V hops merged by log-sum-exp, or (the default while
+ * the gathered K/V fit in 8 GiB) one all-gather of K/V and one attention call
+ * over all keys; AEX_SP_SCHEDULE=ring|gather overrides, the same on every rank. No
  * counterpart exists in the single-device reference, which keeps the full
  * sequence on one device (ParallelSelfAttention.swift:134-136); this computes
  * the same softmax(scale*QK^T)V for the 2048^2 joint sequence (512 text +
@@ -301,14 +304,18 @@ int aex_comm_abort(aex_comm* comm);
  * ranks), the norm weights and the RoPE rows of the shard's tokens; V heads
  * contiguous. Every rank calls it with the same shapes. */
 int aex_ring_attention(aex_ctx* ctx, aex_comm* comm, const aex_attention_args* args, aex_stream stream);
+/* The exchange schedule aex_ring_attention and the sequence-parallel engine take
+ * for `world` shards of `seq` tokens x `heads` heads: 0 ring, 1 all-gather,
+ * -1 bad arguments. */
+int aex_sp_schedule(int world, int seq, int heads);
 
-/* Sequence parallelism for one image over the ranks of `comm` (SURVEY config 5,
- * 2048^2; ImarelloPipeline.swift:921-927 drives one GPU per image): this engine
+/* Sequence parallelism for one image over the ranks of `comm` (the long
+ * sequence, 2048^2; ImarelloPipeline.swift:921-927 drives one GPU per image): this engine
  * was created for one contiguous shard of the joint sequence (cfg.l_txt +
  * cfg.l_img = (l_txt_total + l_img_total) / world rows; all text rows on rank 0,
  * cfg.l_txt = 0 elsewhere; RoPE tables and latents are the shard's rows). Linears
- * and glue stay on the shard; each block's joint attention runs as a ring over
- * all ranks (aex_ring_attention's schedule, NCCL point-to-point); the scheduler
+ * and glue stay on the shard; each block's joint attention runs over all ranks
+ * (aex_ring_attention's schedule, NCCL point-to-point or all-gather); the scheduler
  * uses l_img_total. Every rank makes the same calls in the same order.
  * aex_dit_denoise then launches its steps one by one (no CUDA graph). comm NULL
  * returns the engine to one GPU. */

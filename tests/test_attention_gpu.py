@@ -87,7 +87,7 @@ def test_joint_attention_baseline_configs(cuda_ctx, grid, seed):
     _compare(out, ref, rows)
 
 
-# --- i2i (SURVEY config 5): text 512 + target 64x64 + reference 64x64, J = 8,704 -----------------------
+# --- i2i (image-to-image conditioning): text 512 + target 64x64 + reference 64x64, J = 8,704 -----------------------
 def test_joint_attention_i2i_8704(cuda_ctx):
     """Image-to-image joint sequence: the reference image's tokens carry ids (10, h, w, 0)
     (LatentOps.referenceImageIds, Sources/ImarelloCore/LatentOps.swift:41-45) after the target's

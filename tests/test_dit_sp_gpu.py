@@ -2,9 +2,10 @@
 one-GPU engine on the whole sequence: the small config (hidden 256 = 2 heads,
 1 double + 2 single blocks, 32 text + 8x8 image tokens) split into two equal
 contiguous shards (rank 0: the 32 text rows + 16 image rows; rank 1: 48 image
-rows), joint attention as a ring over NCCL, 3-step denoise. Tolerance:
-relative L2 <= 2e-2 on each rank's latents (bf16 activations; the ring merges
-per-hop bf16 partial outputs by log-sum-exp). Skips with fewer than 2 GPUs."""
+rows), joint attention over NCCL under both exchange schedules (ring; one
+all-gather), 3-step denoise. Tolerance: relative L2 <= 2e-2 on each rank's
+latents (bf16 activations; the ring merges per-hop bf16 partial outputs by
+log-sum-exp). Skips with fewer than 2 GPUs."""
 import ctypes as C
 import datetime
 import os
@@ -40,7 +41,8 @@ def _engine(cfg, ctx, dev, lin, norms, cos, sin, embeds):
     return eng
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, schedule):
+    os.environ["AEX_SP_SCHEDULE"] = schedule  # read at the first sequence-parallel call
     import torch.distributed as dist
 
     from aestrix_b200 import _lib, attention, dit
@@ -91,12 +93,13 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_dit_sequence_parallel_two_gpus(tmp_path):
+@pytest.mark.parametrize("schedule", ["ring", "gather"])
+def test_dit_sequence_parallel_two_gpus(tmp_path, schedule):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
-    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), schedule), nprocs=2, join=True, start_method="spawn")
     for r in range(2):
         rel, finite, status, li = np.load(tmp_path / f"rank{r}.npy")
         assert finite == 1 and status == 0 and li > 0

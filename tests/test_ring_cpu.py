@@ -1,8 +1,13 @@
-"""CPU (gloo, world size 2 and 3) test of the ring-attention algorithm used by
-aex_ring_attention: contiguous sequence shards, K/V passed to rank r+1 each hop,
-partial results merged by their log2-sum-exp, against the full-sequence oracle.
-Mirrors the hop/peer schedule and the merge formula of
-aestrix_b200/csrc/ring_attention.cpp and ring_kernels.cu on numpy arrays."""
+"""CPU (gloo, world size 2 and 3) tests of the two exchange schedules of
+aex_ring_attention against the full-sequence oracle, on contiguous sequence
+shards: the ring (K/V passed to rank r+1 each hop, partial results merged by
+their log2-sum-exp; the hop/peer schedule and merge formula of
+aestrix_b200/csrc/ring_attention.cpp and ring_kernels.cu) and the all-gather
+(every rank's K/V written token-major into slot r of one buffer, gathered in
+place, then one attention over all keys). Also the schedule choice of
+aex_sp_schedule (host logic, no GPU)."""
+import subprocess
+import sys
 import datetime
 import os
 import socket
@@ -67,6 +72,58 @@ def _worker(rank, world, port, S, H, result):
     ref = O.sdpa(q[None], k[None], v[None], 1 / np.sqrt(128))[0]
     result[rank] = float(np.abs(o_acc - ref[sl]).max())
     dist.destroy_process_group()
+
+
+def _gather_worker(rank, world, port, S, H, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    rng = np.random.default_rng(4)
+    q, k, v = (rng.standard_normal((S, H, 128)).astype(np.float32) for _ in range(3))
+    Sp = S // world
+    sl = slice(rank * Sp, (rank + 1) * Sp)
+    # K_all / V_all [world * Sp][H][128]; this rank fills its slot, the gather fills the rest.
+    k_all = torch.zeros(world * Sp, H, 128)
+    v_all = torch.zeros(world * Sp, H, 128)
+    k_all[sl] = torch.from_numpy(k[sl])
+    v_all[sl] = torch.from_numpy(v[sl])
+    for buf in (k_all, v_all):  # in place: rank r's input is its own slot of the output
+        parts = list(buf.view(world, Sp, H, 128).unbind(0))
+        dist.all_gather(parts, parts[rank].clone())
+    assert np.array_equal(k_all.numpy(), k) and np.array_equal(v_all.numpy(), v)
+    o, _ = _partial(q[sl], k_all.numpy(), v_all.numpy(), 1 / np.sqrt(128))
+    ref = O.sdpa(q[None], k[None], v[None], 1 / np.sqrt(128))[0]
+    result[rank] = float(np.abs(o - ref[sl]).max())
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_schedule_gloo(world):
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_gather_worker, args=(world, _free_port(), 96 * world, 2, result), nprocs=world, join=True,
+                       start_method="spawn")
+    assert len(result) == world
+    assert max(result.values()) < 1e-5, dict(result)
+
+
+_SCHEDULE_PROBE = (
+    "import sys; sys.path.insert(0, sys.argv[1]); from aestrix_b200 import _lib; L = _lib.lib(); "
+    "print(L.aex_sp_schedule(8, 2112, 24), L.aex_sp_schedule(2, 8448, 24), L.aex_sp_schedule(8, 1 << 20, 24), "
+    "L.aex_sp_schedule(0, 2112, 24), L.aex_sp_schedule(2, 0, 24))")
+
+
+@pytest.mark.parametrize("env,want", [(None, "1 1 0 -1 -1"), ("ring", "0 0 0 -1 -1"), ("gather", "1 1 1 -1 -1")])
+def test_sp_schedule_choice(env, want):
+    """All-gather while the gathered K/V (2 * world * seq * heads * 256 bytes) fit in 8 GiB, ring beyond;
+    AEX_SP_SCHEDULE overrides. Each case in a fresh process: the override is read once."""
+    e = {k: v for k, v in os.environ.items() if k != "AEX_SP_SCHEDULE"}
+    if env:
+        e["AEX_SP_SCHEDULE"] = env
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", _SCHEDULE_PROBE, root], env=e, capture_output=True, text=True,
+                         timeout=120, check=True).stdout.split()
+    assert " ".join(out) == want
 
 
 @pytest.mark.parametrize("world", [2, 3])

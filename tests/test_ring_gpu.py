@@ -1,6 +1,7 @@
 """aex_ring_attention on 2 GPUs (one process per GPU, NCCL over NVLink) against
 the full-sequence oracle: fused QK-RMSNorm + RoPE + SDPA of the joint sequence
-split into contiguous shards. Skips on a box with fewer than 2 GPUs.
+split into contiguous shards, under both exchange schedules (ring of
+point-to-point hops; one all-gather). Skips on a box with fewer than 2 GPUs.
 Tolerance: relative L2 <= 1e-2, max-abs <= 2e-2 (as the single-GPU attention)."""
 import ctypes as C
 import datetime
@@ -20,7 +21,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, l_txt, grid, heads, out_dir):
+def _worker(rank, world, port, l_txt, grid, heads, out_dir, schedule):
+    os.environ["AEX_SP_SCHEDULE"] = schedule  # read at the first sequence-parallel call
     import torch.distributed as dist
 
     from aestrix_b200 import _lib, attention
@@ -70,13 +72,14 @@ def _worker(rank, world, port, l_txt, grid, heads, out_dir):
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("schedule", ["ring", "gather"])
 @pytest.mark.parametrize("l_txt,grid,heads", [(64, 24, 4), (512, 128, 2)])
-def test_ring_attention_two_gpus(tmp_path, l_txt, grid, heads):
+def test_ring_attention_two_gpus(tmp_path, l_txt, grid, heads, schedule):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
-    mp.start_processes(_worker, args=(2, _free_port(), l_txt, grid, heads, str(tmp_path)), nprocs=2, join=True,
+    mp.start_processes(_worker, args=(2, _free_port(), l_txt, grid, heads, str(tmp_path), schedule), nprocs=2, join=True,
                        start_method="spawn")
     for r in range(2):
         rel, mx, status = np.load(tmp_path / f"rank{r}.npy")
