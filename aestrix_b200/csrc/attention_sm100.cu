@@ -97,8 +97,14 @@ constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
 
 struct Params {
   int seq;       // query rows
-  int seq_kv;    // key/value rows (== seq except for ring-attention hops)
+  int seq_kv;    // key/value rows (== seq except for sequence-parallel calls)
+  // Keys may be split into kv_splits contiguous ranges of n_kv blocks (the
+  // last one shorter, n_kv_total in all), one CTA per (query rows, head,
+  // batch, range); range r of batch b writes its normalized partial output
+  // and log-sum-exp at batch index b * kv_splits + r of O and lse.
   int n_kv;
+  int n_kv_total;
+  int kv_splits;
   float scale_log2;
   // Optional per-row log-sum-exp of the scaled scores in log2 units,
   // lse2 = m + log2(l), stored at lse[b * lse_sb + h * lse_sh + row]; lets
@@ -121,8 +127,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = static_cast<int>(lane_id());
   const int q0 = blockIdx.x * (kTiles * kBM);
   const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int n_kv = p.n_kv;
+  const int ob = blockIdx.z;  // batch index of O and lse
+  const int b = ob / p.kv_splits;
+  const int split = ob - b * p.kv_splits;
+  const int kv_base = split * p.n_kv * kBN;  // first key of this CTA's range
+  const int n_kv = min(p.n_kv, p.n_kv_total - split * p.n_kv);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -174,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (use > 0 && !mbar_wait(&bars[kBarKVEmpty + slot], (use - 1) & 1, &abort_flag, status, kDevTimeoutTma))
           break;
         const CUtensorMap* m = (idx & 1) ? &tm_v : &tm_k;
-        const int kv0 = (idx >> 1) * kBN;
+        const int kv0 = kv_base + (idx >> 1) * kBN;
         uint8_t* dst = smem + kOffKV + slot * kTileBytes;
         mbar_arrive_expect_tx(&bars[kBarKVFull + slot], kTileBytes);
         tma_load_4d(dst, m, &bars[kBarKVFull + slot], 0, kv0, h, b);
@@ -296,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       uint32_t r[128];
-      const int valid = p.seq_kv - j * kBN;
+      const int valid = p.seq_kv - kv_base - j * kBN;
       float mx0, mx1, mx2, mx3;
       auto mask_chunk = [&](int c0) {
         if (valid < kBN) {
@@ -403,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv_l = 1.f / l_run;
       if (p.lse && q0 + t * kBM + row < p.seq)
-        p.lse[b * p.lse_sb + h * p.lse_sh + q0 + t * kBM + row] = m_run + __log2f(l_run);
+        p.lse[ob * p.lse_sb + h * p.lse_sh + q0 + t * kBM + row] = m_run + __log2f(l_run);
 #pragma unroll 1
       for (int cc = 0; cc < 128; cc += 32) {
         uint32_t o[32];
@@ -428,8 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warps of a tile reach this point together or all abort).
     asm volatile("bar.sync %0, %1;" ::"r"(1 + t), "r"(128) : "memory");
     if (ok && quad == 0 && lane == 0 && q0 + t * kBM < p.seq) {
-      tma_store_4d(&tm_o, stage, 0, q0 + t * kBM, h, b);
-      tma_store_4d(&tm_o, stage + kRegionBytes, 64, q0 + t * kBM, h, b);
+      tma_store_4d(&tm_o, stage, 0, q0 + t * kBM, h, ob);
+      tma_store_4d(&tm_o, stage + kRegionBytes, 64, q0 + t * kBM, h, ob);
       bulk_commit_group();
       bulk_wait_group_read0();
     }
@@ -702,18 +711,48 @@ int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratc
                                S, S, H, a->scale, nullptr, 0, 0, stream);
 }
 
+int attention_kv_splits(int ctas, int n_kv, int sms) {
+  if (ctas <= 0 || n_kv <= 0 || sms <= 0) return 1;
+  auto fill = [&](int k) {  // share of the SM slots of the last wave's rounds that hold work
+    const int64_t units = static_cast<int64_t>(ctas) * k;
+    const int64_t waves = (units + sms - 1) / sms;
+    return static_cast<double>(units) / static_cast<double>(waves * sms);
+  };
+  int best = 1;
+  double best_fill = fill(1);
+  for (int k = 2; k <= 4; ++k) {
+    const int per = (n_kv + k - 1) / k;
+    if (per < 8 || (k - 1) * per >= n_kv) break;  // ranges of at least 8 blocks, none empty
+    if (fill(k) > best_fill + 0.05) {  // pays for the merge pass
+      best = k;
+      best_fill = fill(k);
+    }
+  }
+  return best;
+}
+
 int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
                           const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
-                          float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream) {
+                          float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream,
+                          int kv_splits) {
+  const int n_kv_total = (S_kv + attn::kBN - 1) / attn::kBN;
+  if (kv_splits < 1 || B * kv_splits > 65535)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "attention: bad key split count %d", kv_splits);
+  const int per_split = (n_kv_total + kv_splits - 1) / kv_splits;
+  if ((kv_splits - 1) * per_split >= n_kv_total)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "attention: %d key blocks do not fill %d splits", n_kv_total,
+                     kv_splits);
   CUtensorMap tq, tk, tv, to;
   if (int r = bshd_tmap(ctx, &tq, q, qs[0], qs[1], qs[2], B, S, H)) return r;
   if (int r = bshd_tmap(ctx, &tk, k, ks[0], ks[1], ks[2], B, S_kv, H)) return r;
   if (int r = bshd_tmap(ctx, &tv, v, vs[0], vs[1], vs[2], B, S_kv, H)) return r;
-  if (int r = bshd_tmap(ctx, &to, o, os[0], os[1], os[2], B, S, H)) return r;
+  if (int r = bshd_tmap(ctx, &to, o, os[0], os[1], os[2], B * kv_splits, S, H)) return r;
   attn::Params prm{};
   prm.seq = S;
   prm.seq_kv = S_kv;
-  prm.n_kv = (S_kv + attn::kBN - 1) / attn::kBN;
+  prm.n_kv = per_split;
+  prm.n_kv_total = n_kv_total;
+  prm.kv_splits = kv_splits;
   const float sc = scale > 0.f ? scale : 1.0f / std::sqrt(128.0f);
   prm.scale_log2 = sc * 1.4426950408889634f;
   prm.lse = lse;
@@ -722,7 +761,7 @@ int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], cons
   // Per call (cheap): the attribute is per device, and a process may drive several.
   AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(attn::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attn::kSmemBytes));
-  dim3 grid((S + attn::kTiles * attn::kBM - 1) / (attn::kTiles * attn::kBM), H, B);
+  dim3 grid((S + attn::kTiles * attn::kBM - 1) / (attn::kTiles * attn::kBM), H, B * kv_splits);
   attn::attn_fwd_kernel<<<grid, attn::kThreads, attn::kSmemBytes, stream>>>(tq, tk, tv, to, prm, ctx->d_status);
   return check_launch(ctx, "attn_fwd_kernel");
 }

@@ -114,9 +114,18 @@ int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void*
 // The attention kernel on prepared operands: strided [B, S, H, 128] views
 // (strides in elements: batch, seq, head) for Q/O with S rows and K/V with
 // S_kv rows; optional per-row log2-sum-exp output lse[b*lse_sb + h*lse_sh + row].
+// kv_splits > 1 splits the keys into that many contiguous ranges of whole
+// 128-key blocks (every range non-empty), computed by separate CTAs: O and lse
+// then hold B * kv_splits batches (range r of batch b at b * kv_splits + r),
+// each normalized over its own keys, to be combined by merge_splits.
 int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3],
                           const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
-                          float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream);
+                          float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream,
+                          int kv_splits = 1);
+// Key-range count for one attention call of `ctas` CTAs over n_kv key blocks
+// on `sms` SMs: the smallest count that fills whole waves noticeably better
+// than no split (at most 4, every range non-empty), else 1.
+int attention_kv_splits(int ctas, int n_kv, int sms);
 // Sequence-parallel attention internals (ring_attention.cpp) for callers that
 // prepare Q/K themselves. sp_buffers grows this communicator's state for S
 // local rows of H heads and returns where the local operands go: Q head-major

@@ -33,6 +33,11 @@ namespace ring {
 int merge(aex_ctx* ctx, const void* o_h, int64_t oh_ss, int64_t oh_sh, const float* lse_h, const float* lse_in,
           float* lse_out, float* o_acc, int S, int H, bool first, bool final, void* out, int64_t out_ss, int64_t out_sh,
           cudaStream_t s);
+// out = the k key ranges' partial outputs o[r] ([k][S][H][128] bf16, range
+// stride S*H*128) weighted by 2^(lse[r] - lse), lse = log2 sum_r 2^lse[r]
+// (lse: [k][H][S] f32), rounded to bf16 at out[s*out_ss + h*out_sh].
+int merge_splits(aex_ctx* ctx, const void* o, const float* lse, int k, int S, int H, void* out, int64_t out_ss,
+                 int64_t out_sh, cudaStream_t s);
 }
 
 namespace {
@@ -160,7 +165,17 @@ int comm_rank(const aex_comm* c) { return c->rank; }
 // Ring layout: Q plane | K ring[2] (head-major) | V ring[2] (token-major) | O_h bf16 | O_acc f32 | lse_h |
 // lse ping-pong[2] (Q and K ring[0] adjacent: one prep writes both).
 // Gather layout: Q plane (head-major) | K all ranks [P*S][H][128] | V all ranks [P*S][H][128] (token-major;
-// this rank's rows at r*S).
+// this rank's rows at r*S) | with k > 1 key ranges (gather_splits): partial outputs [k][S][H][128] bf16 and
+// their log-sum-exp [k][H][S] f32.
+// Key ranges of the gather schedule's attention call: the local queries (S rows, H heads) over all P*S keys
+// make ceil(S/256)*H CTAs, too few to fill the SMs' waves at short shards (2048^2 at P = 8: 216 CTAs, 1.46
+// waves); splitting the keys fills them (432 CTAs, 2.92 waves) at the cost of one merge pass.
+int gather_splits(const aex_ctx* ctx, int P, int S, int H) {
+  const int ctas = (S + 255) / 256 * H;
+  const int n_kv = (P * S + 127) / 128;
+  return attention_kv_splits(ctas, n_kv, ctx->sm_count);
+}
+
 int sp_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, SpSlots* out) {
   if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
   const int P = c->world, r = c->rank;
@@ -168,7 +183,9 @@ int sp_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, SpSlots* out) {
   if (align256(plane * 2) != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
   uint8_t* base;
   if (use_gather(P, plane * 2)) {
-    if (int e = grow(c, plane * 2 * (1 + 2 * static_cast<size_t>(P)))) return e;
+    const size_t k = static_cast<size_t>(gather_splits(ctx, P, S, H));
+    const size_t parts = k > 1 ? k * plane * 2 + align256(k * H * static_cast<size_t>(S) * 4) : 0;
+    if (int e = grow(c, plane * 2 * (1 + 2 * static_cast<size_t>(P)) + parts)) return e;
     base = static_cast<uint8_t*>(c->buf);
     out->q = reinterpret_cast<uint16_t*>(base);
     out->k = reinterpret_cast<uint16_t*>(base + plane * 2) + r * plane;
@@ -267,9 +284,20 @@ int gather_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, 
   const int64_t q_st[3] = {static_cast<int64_t>(plane), 128, static_cast<int64_t>(S) * 128};  // head-major
   const int64_t kv_st[3] = {static_cast<int64_t>(P) * static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128,
                             128};  // token-major over all ranks
-  const int64_t o_st[3] = {static_cast<int64_t>(S) * out_ss, out_ss, out_sh};
-  return launch_attention_core(ctx, Q, q_st, Kall, kv_st, Vall, kv_st, out, o_st, 1, S, P * S, H, scale, nullptr, 0,
-                               0, s);
+  const int k = gather_splits(ctx, P, S, H);
+  if (k == 1) {
+    const int64_t o_st[3] = {static_cast<int64_t>(S) * out_ss, out_ss, out_sh};
+    return launch_attention_core(ctx, Q, q_st, Kall, kv_st, Vall, kv_st, out, o_st, 1, S, P * S, H, scale, nullptr,
+                                 0, 0, s);
+  }
+  // k key ranges in parallel CTAs, each to its own normalized partial, then one merge.
+  uint16_t* parts = reinterpret_cast<uint16_t*>(base + plane * 2 * (1 + 2 * static_cast<size_t>(P)));
+  float* lse = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(parts) + static_cast<size_t>(k) * plane * 2);
+  const int64_t p_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};  // token-major
+  if (int e = launch_attention_core(ctx, Q, q_st, Kall, kv_st, Vall, kv_st, parts, p_st, 1, S, P * S, H, scale, lse,
+                                    static_cast<int64_t>(H) * S, S, s, k))
+    return e;
+  return ring::merge_splits(ctx, parts, lse, k, S, H, out, out_ss, out_sh, s);
 }
 
 }  // namespace

@@ -1,7 +1,9 @@
 """aex_ring_attention on 2 GPUs (one process per GPU, NCCL over NVLink) against
 the full-sequence oracle: fused QK-RMSNorm + RoPE + SDPA of the joint sequence
 split into contiguous shards, under both exchange schedules (ring of
-point-to-point hops; one all-gather). Skips on a box with fewer than 2 GPUs.
+point-to-point hops; one all-gather); the 2-rank cases skip on a box with
+fewer than 2 GPUs. On one GPU, a 1-rank communicator runs the all-gather
+schedule's attention split into key ranges.
 Tolerance: relative L2 <= 1e-2, max-abs <= 2e-2 (as the single-GPU attention)."""
 import ctypes as C
 import datetime
@@ -85,3 +87,46 @@ def test_ring_attention_two_gpus(tmp_path, l_txt, grid, heads, schedule):
         rel, mx, status = np.load(tmp_path / f"rank{r}.npy")
         assert status == 0
         assert rel <= 1e-2 and mx <= 2e-2, f"rank {r}: rel-L2 {rel:.3e} max-abs {mx:.3e}"
+
+
+def test_single_rank_gather_with_key_ranges():
+    """One GPU, a 1-rank communicator: the gather schedule's attention over a 2,112-row shard with 24 heads
+    (216 CTAs, under 1.5 waves of 148 SMs) runs as two key ranges merged by log-sum-exp (aex_sp_schedule says
+    gather; the split is chosen from the SM count). Against the oracle on 64 rows, same tolerance."""
+    from aestrix_b200 import _lib, attention
+    from oracle import oracle as O
+
+    L = _lib.lib()
+    ctx = _lib.Context(0)
+    dev = torch.device("cuda", 0)
+    uid = (C.c_char * 128)()
+    ctx.check(L.aex_comm_unique_id(uid))
+    comm = C.c_void_p()
+    ctx.check(L.aex_comm_create(ctx.handle, 1, 0, uid, 60000, C.byref(comm)))
+    try:
+        S, H = 2112, 24
+        assert L.aex_sp_schedule(1, S, H) == 1
+        g = torch.Generator().manual_seed(9)
+        q, k, v = (torch.randn(1, S, H, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+        wq = (1 + 0.1 * torch.randn(128, generator=g)).float()
+        wk = (1 + 0.1 * torch.randn(128, generator=g)).float()
+        ang = (torch.rand(S, 64, generator=g) * 6.2831853).double()
+        cos, sin = torch.cos(ang).float(), torch.sin(ang).float()
+        qd, kd, vd = (t.to(dev) for t in (q, k, v))
+        out = torch.empty_like(qd)
+        a = attention.make_args(qd, kd, vd, out, "bshd", wq.to(dev), wk.to(dev), 1e-5, cos.to(dev), sin.to(dev))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for _ in range(2):
+            ctx.check(L.aex_ring_attention(ctx.handle, comm, C.byref(a), stream))
+        ctx.sync(stream, timeout_ms=60000)
+        assert ctx.device_status() == 0
+        args = (q.float().numpy(), k.float().numpy(), v.float().numpy(), wq.numpy(), wk.numpy(), 1e-5,
+                cos.numpy(), sin.numpy())
+        ref = np.concatenate([O.joint_attention(*args, q_begin=0, q_end=32)[:, :32],
+                              O.joint_attention(*args, q_begin=S - 32, q_end=S)[:, S - 32:]], 1)
+        got = out.float().cpu().numpy()[:, np.r_[0:32, S - 32:S]]
+        d = got - ref
+        rel = float(np.linalg.norm(d) / np.linalg.norm(ref))
+        assert rel <= 1e-2 and float(np.abs(d).max()) <= 2e-2, f"rel-L2 {rel:.3e} max-abs {np.abs(d).max():.3e}"
+    finally:
+        L.aex_comm_destroy(comm)
