@@ -367,8 +367,7 @@ def measure_dit(ctx, dev, world, runs=3):
     fl = dit.dit_flops(cfg)
     ok = bool(torch.isfinite(lat).all().item())
     eng.close()
-    schedule = {0: "ring", 1: "all-gather"}.get(_lib.lib().aex_sp_schedule(world, Jp, full.heads), "?")
-    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "schedule": schedule, "images_per_s": world * 4000.0 / ms / 4,
+    return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "images_per_s": world * 4000.0 / ms / 4,
             "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12, "tflop_per_step": fl["total"] / 1e12,
             "flops_split_per_step": {"linear": fl["linear"] / 1e12, "attention": fl["attention"] / 1e12},
             "n_gpus": world, "batch": world, "finite": ok,
