@@ -119,6 +119,7 @@ _SIGNATURES = [
     ("aex_comm_abort", C.c_int, [_VP]),
     ("aex_ring_attention", C.c_int, [_VP, _VP, C.POINTER(aex_attention_args), _VP]),
     ("aex_sp_schedule", C.c_int, [C.c_int, C.c_int, C.c_int]),
+    ("aex_sp_key_ranges", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int]),
     ("aex_selftest_umma", C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
 ]
 

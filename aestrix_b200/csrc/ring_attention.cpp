@@ -170,11 +170,13 @@ int comm_rank(const aex_comm* c) { return c->rank; }
 // Key ranges of the gather schedule's attention call: the local queries (S rows, H heads) over all P*S keys
 // make ceil(S/256)*H CTAs, too few to fill the SMs' waves at short shards (2048^2 at P = 8: 216 CTAs, 1.46
 // waves); splitting the keys fills them (432 CTAs, 2.92 waves) at the cost of one merge pass.
-int gather_splits(const aex_ctx* ctx, int P, int S, int H) {
+int key_ranges(int P, int S, int H, int sms) {
   const int ctas = (S + 255) / 256 * H;
   const int n_kv = (P * S + 127) / 128;
-  return attention_kv_splits(ctas, n_kv, ctx->sm_count);
+  return attention_kv_splits(ctas, n_kv, sms);
 }
+
+int gather_splits(const aex_ctx* ctx, int P, int S, int H) { return key_ranges(P, S, H, ctx->sm_count); }
 
 int sp_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, SpSlots* out) {
   if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
@@ -390,6 +392,11 @@ int aex_comm_abort(aex_comm* c) {
   ncclResult_t r = nccl().commAbort(c->comm);
   c->comm = nullptr;
   return r == ncclSuccess ? AEX_OK : AEX_ERR_NCCL;
+}
+
+int aex_sp_key_ranges(int world, int seq, int heads, int sms) {
+  if (world < 1 || seq <= 0 || heads <= 0 || sms <= 0) return -1;
+  return aex::key_ranges(world, seq, heads, sms);
 }
 
 int aex_sp_schedule(int world, int seq, int heads) {

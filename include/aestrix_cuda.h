@@ -308,6 +308,11 @@ int aex_ring_attention(aex_ctx* ctx, aex_comm* comm, const aex_attention_args* a
  * for `world` shards of `seq` tokens x `heads` heads: 0 ring, 1 all-gather,
  * -1 bad arguments. */
 int aex_sp_schedule(int world, int seq, int heads);
+/* Key ranges the all-gather schedule's attention call splits into on a device
+ * of `sms` SMs (1: no split; at most 4), chosen so the CTAs of a short shard
+ * fill whole waves: 2048^2 at world 8 (2,112 rows, 24 heads) on 148 SMs gives
+ * 2. -1 for bad arguments. */
+int aex_sp_key_ranges(int world, int seq, int heads, int sms);
 
 /* Sequence parallelism for one image over the ranks of `comm` (the long
  * sequence, 2048^2; ImarelloPipeline.swift:921-927 drives one GPU per image): this engine

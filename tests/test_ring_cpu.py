@@ -126,6 +126,21 @@ def test_sp_schedule_choice(env, want):
     assert " ".join(out) == want
 
 
+@pytest.mark.parametrize("world,seq,heads,sms,want", [
+    (8, 2112, 24, 148, 2),   # 216 CTAs = 1.46 waves -> 432 = 2.92
+    (4, 4224, 24, 148, 1),   # 408 CTAs = 2.76 waves: a split fills no better
+    (2, 8448, 24, 148, 2),   # 792 CTAs = 5.35 waves -> 1584 = 10.7
+    (1, 384, 2, 148, 1),     # 3 key blocks: no range of at least 8 blocks
+    (0, 2112, 24, 148, -1),  # bad arguments
+    (8, 2112, 24, 0, -1),
+])
+def test_sp_key_ranges(world, seq, heads, sms, want):
+    """Key ranges of the gather schedule's attention: the smallest split (<= 4) whose wave fill beats no split
+    by more than 5 points, ranges of at least 8 key blocks."""
+    from aestrix_b200 import _lib
+    assert _lib.lib().aex_sp_key_ranges(world, seq, heads, sms) == want
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_ring_schedule_and_merge_gloo(world):
     ctx = mp.get_context("spawn")
