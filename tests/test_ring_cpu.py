@@ -126,6 +126,26 @@ def test_sp_schedule_choice(env, want):
     assert " ".join(out) == want
 
 
+@pytest.mark.parametrize("k", [2, 3, 4])
+def test_key_range_merge(k):
+    """The gather schedule's split attention: k contiguous key ranges, each a normalized partial with its
+    log2-sum-exp, combined as sum_r 2^(lse_r - max) o_r / sum_r 2^(lse_r - max) (merge_splits_kernel in
+    aestrix_b200/csrc/ring_kernels.cu), equals attention over all keys."""
+    rng = np.random.default_rng(11 + k)
+    S, T, H = 40, 128 * 3 * k + 37, 2  # 3k + 1 key blocks, the last one ragged
+    q, kk, v = (rng.standard_normal((n, H, 128)).astype(np.float32) for n in (S, T, T))
+    blocks = (T + 127) // 128
+    per = -(-blocks // k)  # whole 128-key blocks per range, every range non-empty
+    assert (k - 1) * per < blocks
+    rng_keys = [slice(r * per * 128, min(T, (r + 1) * per * 128)) for r in range(k)]
+    parts = [_partial(q, kk[sl], v[sl], 1 / np.sqrt(128)) for sl in rng_keys]
+    lse = np.stack([p[1] for p in parts])  # [k, H, S]
+    w = np.exp2(lse - lse.max(0, keepdims=True))
+    out = sum(w[r].T[..., None] * parts[r][0] for r in range(k)) / w.sum(0).T[..., None]
+    ref = _partial(q, kk, v, 1 / np.sqrt(128))[0]
+    assert float(np.abs(out - ref).max()) < 1e-5
+
+
 @pytest.mark.parametrize("world,seq,heads,sms,want", [
     (8, 2112, 24, 148, 2),   # 216 CTAs = 1.46 waves -> 432 = 2.92
     (4, 4224, 24, 148, 1),   # 408 CTAs = 2.76 waves: a split fills no better
