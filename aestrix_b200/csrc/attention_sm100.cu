@@ -596,10 +596,10 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
 }  // namespace attn
 
 namespace {
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
 
-int validate(aex_ctx* ctx, const aex_attention_args* a) {
+int validate_attention_args(aex_ctx* ctx, const aex_attention_args* a) {
   if (!a) return set_error(ctx, AEX_ERR_INVALID_ARG, "args is NULL");
   if (a->head_dim != 128)
     return set_error(ctx, AEX_ERR_UNSUPPORTED, "head_dim %d unsupported (only 128)", a->head_dim);
@@ -627,6 +627,8 @@ int validate(aex_ctx* ctx, const aex_attention_args* a) {
     return set_error(ctx, AEX_ERR_INVALID_ARG, "eps must be >= 0");
   return AEX_OK;
 }
+
+namespace {
 
 bool needs_prep(const aex_attention_args* a) {
   return a->norm_q_weight || a->norm_k_weight || a->rope_cos;
@@ -780,7 +782,7 @@ int aex_joint_attention_ws(aex_ctx* ctx, const aex_attention_args* args, void* s
                            aex_stream stream) {
   using namespace aex;
   if (!ctx) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL ctx");
-  if (int r = validate(ctx, args)) return r;
+  if (int r = validate_attention_args(ctx, args)) return r;
   if (int r = bind_device(ctx)) return r;
   return joint_attention_impl(ctx, args, scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
@@ -788,7 +790,7 @@ int aex_joint_attention_ws(aex_ctx* ctx, const aex_attention_args* args, void* s
 int aex_joint_attention(aex_ctx* ctx, const aex_attention_args* args, aex_stream stream) {
   using namespace aex;
   if (!ctx) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL ctx");
-  if (int r = validate(ctx, args)) return r;
+  if (int r = validate_attention_args(ctx, args)) return r;
   if (int r = bind_device(ctx)) return r;
   const size_t need = aex_joint_attention_scratch_bytes(args);
   void* ws = nullptr;
@@ -842,7 +844,7 @@ int noalloc_scratch(aex_ctx* ctx, void** out) {
 extern "C" int aex_joint_attention_noalloc(aex_ctx* ctx, const aex_attention_args* args, aex_stream stream) {
   using namespace aex;
   if (!ctx) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL ctx");
-  if (int r = validate(ctx, args)) return r;
+  if (int r = validate_attention_args(ctx, args)) return r;
   const size_t need = aex_joint_attention_scratch_bytes(args);
   if (need > kNoAllocScratchBytes)
     return set_error(ctx, AEX_ERR_INVALID_ARG,

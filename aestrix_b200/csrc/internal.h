@@ -147,6 +147,10 @@ int sp_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int6
            cudaStream_t s);
 // The context a DiT engine was created on.
 aex_ctx* dit_context(aex_dit* d);
+// The checks every attention entry point applies to its args (shapes, NULL
+// and 16-byte-aligned pointers, strides, paired rope tables, eps); AEX_OK or
+// AEX_ERR_INVALID_ARG / AEX_ERR_UNSUPPORTED with the message set.
+int validate_attention_args(aex_ctx* ctx, const aex_attention_args* a);
 // Attention (and prep if args ask for it) on validated args.
 int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
                          cudaStream_t stream);

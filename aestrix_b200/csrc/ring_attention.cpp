@@ -13,7 +13,9 @@
 //    r+1 / ncclRecv from r-1 on a dedicated stream, double buffered); partial
 //    outputs merged by their log-sum-exp (ring_kernels.cu);
 //  * gather: one ncclAllGather of every rank's K and V (token-major, in place)
-//    and one attention call of the local queries over all P*S keys.
+//    and one attention call of the local queries over all P*S keys (its keys
+//    split into ranges merged by log-sum-exp when a short shard's CTAs would
+//    underfill the SMs' waves).
 //
 // NCCL is resolved at run time (the copy already loaded in the process, else
 // libnccl.so.2), so the library has no link-time NCCL dependency.
@@ -131,7 +133,7 @@ struct aex_comm {
   int world = 0, rank = 0;
   cudaStream_t stream = nullptr;  // exchange stream
   cudaEvent_t ev_attn[2] = {nullptr, nullptr}, ev_recv = nullptr, ev_start = nullptr;
-  // ring state, grown on demand
+  // exchange state (ring or gather layout), grown on demand
   void* buf = nullptr;
   size_t buf_bytes = 0;
 };
@@ -163,7 +165,7 @@ int comm_world(const aex_comm* c) { return c->world; }
 int comm_rank(const aex_comm* c) { return c->rank; }
 
 // Ring layout: Q plane | K ring[2] (head-major) | V ring[2] (token-major) | O_h bf16 | O_acc f32 | lse_h |
-// lse ping-pong[2] (Q and K ring[0] adjacent: one prep writes both).
+// lse ping-pong[2]; this rank's Q and K are prepared into the Q plane and K ring[0].
 // Gather layout: Q plane (head-major) | K all ranks [P*S][H][128] | V all ranks [P*S][H][128] (token-major;
 // this rank's rows at r*S) | with k > 1 key ranges (gather_splits): partial outputs [k][S][H][128] bf16 and
 // their log-sum-exp [k][H][S] f32.
@@ -408,9 +410,8 @@ int aex_ring_attention(aex_ctx* ctx, aex_comm* c, const aex_attention_args* a, a
   using namespace aex;
   if (!ctx || !c || !a) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL argument");
   if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
-  if (a->head_dim != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "head_dim must be 128");
+  if (int r = validate_attention_args(ctx, a)) return r;
   if (a->batch != 1) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention takes batch 1");
-  if (a->seq <= 0 || a->heads <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "seq/heads must be positive");
   if (a->v.stride_h != 128) return set_error(ctx, AEX_ERR_UNSUPPORTED, "ring attention needs V heads contiguous");
   if (int r = bind_device(ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);

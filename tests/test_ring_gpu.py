@@ -130,3 +130,32 @@ def test_single_rank_gather_with_key_ranges():
         assert rel <= 1e-2 and float(np.abs(d).max()) <= 2e-2, f"rel-L2 {rel:.3e} max-abs {np.abs(d).max():.3e}"
     finally:
         L.aex_comm_destroy(comm)
+
+
+def test_sequence_parallel_call_rejects_bad_args():
+    """aex_ring_attention applies the same argument checks as aex_joint_attention before any launch: a NULL or
+    misaligned tensor comes back as AEX_ERR_INVALID_ARG with a message, not as a device fault."""
+    from aestrix_b200 import _lib, attention
+
+    L = _lib.lib()
+    ctx = _lib.Context(0)
+    dev = torch.device("cuda", 0)
+    uid = (C.c_char * 128)()
+    ctx.check(L.aex_comm_unique_id(uid))
+    comm = C.c_void_p()
+    ctx.check(L.aex_comm_create(ctx.handle, 1, 0, uid, 60000, C.byref(comm)))
+    try:
+        q, k, v = (torch.randn(1, 256, 2, 128, device=dev).to(torch.bfloat16) for _ in range(3))
+        out = torch.empty_like(q)
+        a = attention.make_args(q, k, v, out, "bshd")
+        a.q.data = None
+        rc = L.aex_ring_attention(ctx.handle, comm, C.byref(a), None)
+        assert rc == _lib.AEX_ERR_INVALID_ARG
+        assert b"q.data" in L.aex_last_error_string(ctx.handle)
+        a = attention.make_args(q, k, v, out, "bshd")
+        a.k.data = k.data_ptr() + 2  # not 16-byte aligned
+        rc = L.aex_ring_attention(ctx.handle, comm, C.byref(a), None)
+        assert rc == _lib.AEX_ERR_INVALID_ARG
+        assert ctx.device_status() == 0
+    finally:
+        L.aex_comm_destroy(comm)
