@@ -620,6 +620,8 @@ int aex_dit_set_timestep(aex_dit* d, float timestep, aex_stream stream) {
 int aex_dit_forward(aex_dit* d, const float* latents, float* velocity, aex_stream stream) {
   using namespace aex;
   if (!d || !latents || !velocity) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if ((reinterpret_cast<uintptr_t>(latents) | reinterpret_cast<uintptr_t>(velocity)) & 3)
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "latents and velocity must be 4-byte aligned f32 arrays");
   if (int r = bind_device(d->ctx)) return r;
   return forward(d, latents, velocity, static_cast<cudaStream_t>(stream));
 }
@@ -627,6 +629,8 @@ int aex_dit_forward(aex_dit* d, const float* latents, float* velocity, aex_strea
 int aex_dit_denoise_step(aex_dit* d, const float* lat_in, float* lat_out, float dt, aex_stream stream) {
   using namespace aex;
   if (!d || !lat_in || !lat_out) return set_error(d ? d->ctx : nullptr, AEX_ERR_INVALID_ARG, "NULL argument");
+  if ((reinterpret_cast<uintptr_t>(lat_in) | reinterpret_cast<uintptr_t>(lat_out)) & 3)
+    return set_error(d->ctx, AEX_ERR_INVALID_ARG, "latents must be 4-byte aligned f32 arrays");
   if (int r = bind_device(d->ctx)) return r;
   auto s = static_cast<cudaStream_t>(stream);
   AEX_TRY(glue::set_scalar(d->ctx, d->CUR + 1, dt, s));
