@@ -12,8 +12,9 @@
 //  * qk_prep_kernel — one half-warp per (operand, batch, token, head) row: f32
 //    RMSNorm over the 128-wide head with the learned weight, then the
 //    interleaved-pair rotation with the row's cos/sin, rounded once to bf16
-//    into head-major scratch [B][H][S][128] (TMA-friendly: a 128-row tile is
-//    one contiguous 32 KB block). HBM-bound.
+//    into scratch: token-major [B][S][H][128] for the fused call (the input's
+//    row order, so its writes are sequential), head-major [B][H][S][128] for
+//    the sequence-parallel slots. HBM-bound.
 //  * attn_fwd_kernel — one CTA per (256 query rows, head, batch), 12 warps:
 //      warps 0-3   softmax warpgroup of query tile 0 (one query row per thread)
 //      warps 4-7   softmax warpgroup of query tile 1
@@ -469,9 +470,10 @@ struct PrepParams {
   const float* sin_t;
   float eps;
   int batch, seq, heads;
-  __nv_bfloat16* out;    // Q (and K when k_out is NULL): [2][B][H][S][128]
+  __nv_bfloat16* out;    // Q (and K when k_out is NULL): [2][B][H][S][128], or [2][B][S][H][128] when out_token_major
   __nv_bfloat16* k_out;  // K elsewhere: [B][H][S][128], or [B][S][H][128] when k_token_major
   int k_token_major;
+  int out_token_major;
 };
 
 // Each half-warp owns one 128-wide row (16 lanes x 8 elements = one 16-byte
@@ -579,8 +581,9 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepParams p) {
     }
     if (valid) {
       __nv_bfloat16* base = p.out;
-      int64_t dst = static_cast<int64_t>(c.which) * rows_per_op * kD +
-                    (static_cast<int64_t>(c.b * heads + c.h) * seq + c.s) * kD;
+      const int64_t in_op = p.out_token_major ? static_cast<int64_t>(c.b * seq + c.s) * heads + c.h
+                                              : static_cast<int64_t>(c.b * heads + c.h) * seq + c.s;
+      int64_t dst = static_cast<int64_t>(c.which) * rows_per_op * kD + in_op * kD;
       if (c.which && p.k_out) {
         base = p.k_out;
         dst = p.k_token_major ? (static_cast<int64_t>(c.b * seq + c.s) * heads + c.h) * kD
@@ -649,7 +652,7 @@ int bshd_tmap(aex_ctx* ctx, CUtensorMap* m, const void* base, int64_t sb, int64_
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
                    int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
                    float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream, void* k_out,
-                   bool k_token_major) {
+                   bool k_token_major, bool out_token_major) {
   if (B <= 0 || S <= 0 || H <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "qk prep: empty batch, seq or heads");
   attn::PrepParams pp{};
   pp.q = static_cast<const __nv_bfloat16*>(q);
@@ -674,6 +677,7 @@ int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void*
   pp.out = static_cast<__nv_bfloat16*>(out);
   pp.k_out = static_cast<__nv_bfloat16*>(k_out);
   pp.k_token_major = k_token_major ? 1 : 0;
+  pp.out_token_major = out_token_major ? 1 : 0;
   const int64_t rows = 2ll * B * S * H;
   const int64_t per_block = attn::kPrepWarps * attn::kPrepRowsPerWarp;
   const int64_t blocks = (rows + per_block - 1) / per_block;
@@ -696,15 +700,19 @@ int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratc
                        need);
     if (reinterpret_cast<uintptr_t>(scratch) % 256)
       return set_error(ctx, AEX_ERR_INVALID_ARG, "scratch must be 256-byte aligned");
+    // Token-major scratch: the same row order as the inputs, so the prep writes sequentially (measured about
+    // 1 % faster per fused call at 1024^2 than head-major, the values identical); the attention kernel's TMA
+    // reads 128-token boxes of one head with an H*256-byte row pitch either way.
     if (int r = launch_qk_prep(ctx, a->q.data, qs, a->k.data, ks, B, S, H, a->norm_q_weight, a->norm_k_weight,
-                               nullptr, nullptr, 0, a->eps, a->rope_cos, a->rope_sin, scratch, stream))
+                               nullptr, nullptr, 0, a->eps, a->rope_cos, a->rope_sin, scratch, stream, nullptr, false,
+                               true))
       return r;
     const int64_t plane = static_cast<int64_t>(B) * H * S * 128;
     qsrc = scratch;
     ksrc = static_cast<const __nv_bfloat16*>(scratch) + plane;
     qs[0] = static_cast<int64_t>(H) * S * 128;
-    qs[1] = 128;
-    qs[2] = static_cast<int64_t>(S) * 128;
+    qs[1] = static_cast<int64_t>(H) * 128;
+    qs[2] = 128;
     ks[0] = qs[0];
     ks[1] = qs[1];
     ks[2] = qs[2];

@@ -105,12 +105,13 @@ int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s);
 // the matching 128 up rows, for the SwiGLU epilogue.
 int qmm_glu_interleave(aex_ctx* ctx, const aex_qweight* src, int plain_rows, int mlp, aex_qweight** out,
                        cudaStream_t s);
-// QK-RMSNorm + RoPE pre-pass into head-major scratch [2][B][H][S][128]; tokens
-// s < split use (wq_a, wk_a), the others (wq, wk).
+// QK-RMSNorm + RoPE pre-pass into scratch [2][B][H][S][128] (head-major), or
+// [2][B][S][H][128] with out_token_major; K goes to k_out instead when given.
+// Tokens s < split use (wq_a, wk_a), the others (wq, wk).
 int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void* k, const int64_t ks[3], int B, int S,
                    int H, const float* wq, const float* wk, const float* wq_a, const float* wk_a, int split,
                    float eps, const float* cos_t, const float* sin_t, void* out, cudaStream_t stream,
-                   void* k_out = nullptr, bool k_token_major = false);
+                   void* k_out = nullptr, bool k_token_major = false, bool out_token_major = false);
 // The attention kernel on prepared operands: strided [B, S, H, 128] views
 // (strides in elements: batch, seq, head) for Q/O with S rows and K/V with
 // S_kv rows; optional per-row log2-sum-exp output lse[b*lse_sb + h*lse_sh + row].
