@@ -72,6 +72,24 @@ class aex_attention_args(C.Structure):
     ]
 
 
+class aex_sp_op(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("kind", "send_to", "recv_from", "slot", "part", "wait_exchange", "stream")]
+
+
+AEX_SP_OP_EXCHANGE, AEX_SP_OP_ATTEND, AEX_SP_OP_MERGE = 0, 1, 2
+
+
+def sp_plan(world: int, rank: int) -> list[aex_sp_op]:
+    """The overlap schedule's steps for `rank` (aex_sp_plan)."""
+    n = lib().aex_sp_plan(world, rank, None, 0)
+    if n < 0:
+        raise ValueError(f"no overlap plan for world {world} rank {rank}")
+    ops = (aex_sp_op * n)()
+    if lib().aex_sp_plan(world, rank, ops, n) != n:
+        raise RuntimeError("aex_sp_plan")
+    return list(ops)
+
+
 class aex_dit_config(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("hidden", "heads", "n_double", "n_single", "mlp_hidden", "in_channels",
                                        "text_dim", "timestep_dim", "l_txt", "l_img")] + [
@@ -100,6 +118,7 @@ _SIGNATURES = [
     ("aex_qweight_shape", C.c_int, [_VP, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     ("aex_qweight_dequantize", C.c_int, [_VP, _VP, _VP, _VP]),
     ("aex_qmm", C.c_int, [_VP, _VP, _VP, C.c_int64, C.c_int, _VP, C.c_int64, C.c_int, _VP]),
+    ("aex_qmm_ex", C.c_int, [_VP, _VP, _VP, C.c_int, C.c_int64, C.c_int, _VP, C.c_int64, C.c_int, _VP]),
     ("aex_dit_create", C.c_int, [_VP, C.POINTER(aex_dit_config), C.POINTER(_VP)]),
     ("aex_dit_destroy", None, [_VP]),
     ("aex_dit_load_linear", C.c_int, [_VP, C.c_char_p, _VP, _VP, _VP, C.c_int, C.c_int, _VP]),
@@ -120,7 +139,9 @@ _SIGNATURES = [
     ("aex_ring_attention", C.c_int, [_VP, _VP, C.POINTER(aex_attention_args), _VP]),
     ("aex_sp_schedule", C.c_int, [C.c_int, C.c_int, C.c_int]),
     ("aex_sp_key_ranges", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    ("aex_sp_plan", C.c_int, [C.c_int, C.c_int, _VP, C.c_int]),
     ("aex_selftest_umma", C.c_int, [_VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
+    ("aex_selftest_wait", C.c_int, [_VP, C.c_int, _VP]),
 ]
 
 _lib = None

@@ -686,20 +686,34 @@ int launch_qk_prep(aex_ctx* ctx, const void* q, const int64_t qs[3], const void*
   return check_launch(ctx, "qk_prep_kernel");
 }
 
+namespace {
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// Scratch of a key-split call: k partial outputs per batch [B][k][S][H][128] bf16, then their
+// log2-sum-exp [B][k][H][S] f32.
+size_t split_scratch_bytes(int B, int S, int H, int k) {
+  if (k <= 1) return 0;
+  const size_t rows = static_cast<size_t>(B) * k * S * H;
+  return align256(rows * 256) + align256(rows * 4);
+}
+}  // namespace
+
 int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, int kv_splits) {
   const int B = a->batch, S = a->seq, H = a->heads;
   const void* qsrc = a->q.data;
   const void* ksrc = a->k.data;
   int64_t qs[3] = {a->q.stride_b, a->q.stride_s, a->q.stride_h};
   int64_t ks[3] = {a->k.stride_b, a->k.stride_s, a->k.stride_h};
-  if (needs_prep(a)) {
-    const size_t need = aex_joint_attention_scratch_bytes(a);
+  const size_t qk_need = aex_joint_attention_scratch_bytes(a);
+  const size_t need = align256(qk_need) + split_scratch_bytes(B, S, H, kv_splits);
+  if (need > 0) {
     if (!scratch || scratch_bytes < need)
       return set_error(ctx, AEX_ERR_INVALID_ARG, "scratch of %zu bytes is smaller than the %zu needed", scratch_bytes,
                        need);
     if (reinterpret_cast<uintptr_t>(scratch) % 256)
       return set_error(ctx, AEX_ERR_INVALID_ARG, "scratch must be 256-byte aligned");
+  }
+  if (needs_prep(a)) {
     // Token-major scratch: the same row order as the inputs, so the prep writes sequentially (measured about
     // 1 % faster per fused call at 1024^2 than head-major, the values identical); the attention kernel's TMA
     // reads 128-token boxes of one head with an H*256-byte row pitch either way.
@@ -717,8 +731,33 @@ int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratc
     ks[1] = qs[1];
     ks[2] = qs[2];
   }
-  return launch_attention_core(ctx, qsrc, qs, ksrc, ks, a->v.data, &a->v.stride_b, a->out.data, &a->out.stride_b, B,
-                               S, S, H, a->scale, nullptr, 0, 0, stream);
+  if (kv_splits <= 1)
+    return launch_attention_core(ctx, qsrc, qs, ksrc, ks, a->v.data, &a->v.stride_b, a->out.data, &a->out.stride_b, B,
+                                 S, S, H, a->scale, nullptr, 0, 0, stream);
+  // Keys in kv_splits contiguous ranges run by separate CTAs of one launch (each range's normalized partial
+  // output and log-sum-exp), then one merge pass per batch into the caller's output.
+  const int k = kv_splits;
+  uint8_t* base = static_cast<uint8_t*>(scratch) + align256(qk_need);
+  uint16_t* parts = reinterpret_cast<uint16_t*>(base);
+  float* lse = reinterpret_cast<float*>(base + align256(static_cast<size_t>(B) * k * S * H * 256));
+  const int64_t plane1 = static_cast<int64_t>(S) * H * 128;  // one range of one batch
+  const int64_t p_st[3] = {plane1, static_cast<int64_t>(H) * 128, 128};
+  if (int r = launch_attention_core(ctx, qsrc, qs, ksrc, ks, a->v.data, &a->v.stride_b, parts, p_st, B, S, S, H,
+                                    a->scale, lse, static_cast<int64_t>(H) * S, S, stream, k))
+    return r;
+  for (int b = 0; b < B; ++b) {
+    if (int r = ring::merge_splits(ctx, parts + static_cast<int64_t>(b) * k * plane1, plane1, p_st[1], p_st[2],
+                                   lse + static_cast<int64_t>(b) * k * H * S, static_cast<int64_t>(H) * S, k, S, H,
+                                   static_cast<uint16_t*>(a->out.data) + static_cast<int64_t>(b) * a->out.stride_b,
+                                   a->out.stride_s, a->out.stride_h, stream))
+      return r;
+  }
+  return AEX_OK;
+}
+
+int fused_kv_splits(const aex_ctx* ctx, int B, int S, int H) {
+  const int ctas = (S + 2 * 128 - 1) / (2 * 128) * H * B;
+  return attention_kv_splits(ctas, (S + 127) / 128, ctx->sm_count);
 }
 
 int attention_kv_splits(int ctas, int n_kv, int sms) {
@@ -800,10 +839,14 @@ int aex_joint_attention(aex_ctx* ctx, const aex_attention_args* args, aex_stream
   if (!ctx) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL ctx");
   if (int r = validate_attention_args(ctx, args)) return r;
   if (int r = bind_device(ctx)) return r;
-  const size_t need = aex_joint_attention_scratch_bytes(args);
+  // A call whose CTAs (256 query rows x head x batch) would underfill the SMs' waves (a few heads, e.g. a
+  // head-sharded call, or a short sequence) splits its keys into ranges merged by log-sum-exp.
+  const int k = fused_kv_splits(ctx, args->batch, args->seq, args->heads);
+  const size_t need = align256(aex_joint_attention_scratch_bytes(args)) +
+                      split_scratch_bytes(args->batch, args->seq, args->heads, k);
   void* ws = nullptr;
   if (int r = ensure_scratch(ctx, need, &ws)) return r;
-  return joint_attention_impl(ctx, args, ws, need, static_cast<cudaStream_t>(stream));
+  return joint_attention_impl(ctx, args, ws, need, static_cast<cudaStream_t>(stream), k);
 }
 
 }  // extern "C"
@@ -826,21 +869,47 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 64ull << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch per device ordinal, resolved once with
-// that device current (host code must not pass the host-side symbol itself).
+// Device address of g_noalloc_scratch per device ordinal, resolved with that
+// device current (host code must not pass the host-side symbol itself) at the
+// first call on the device, together with the CUDA context it was resolved
+// in. A later call in another context of the device (after cudaDeviceReset
+// tore the primary context down and a new one was created) resolves it again,
+// so a stale address is never launched on.
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kMaxDevices] = {};
+CUcontext g_noalloc_cu_ctx[kMaxDevices] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 
 int noalloc_scratch(aex_ctx* ctx, void** out) {
   if (ctx->device < 0 || ctx->device >= kMaxDevices)
     return set_error(ctx, AEX_ERR_UNSUPPORTED, "device ordinal %d beyond %d", ctx->device, kMaxDevices);
+  // Since CUDA 12 cudaSetDevice makes the device's primary context current (initializing it if needed).
+  AEX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  CUcontext cur = nullptr;
+  auto get_ctx = ctx_get_current_fn();
+  if (!get_ctx || get_ctx(&cur) != CUDA_SUCCESS || !cur)
+    return set_error(ctx, AEX_ERR_CUDA, "cuCtxGetCurrent failed: no current CUDA context for device %d", ctx->device);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[ctx->device]) {
+  if (!g_noalloc_addr[ctx->device] || g_noalloc_cu_ctx[ctx->device] != cur) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_error(ctx, e, "cudaGetSymbolAddress(g_noalloc_scratch)");
     g_noalloc_addr[ctx->device] = p;
+    g_noalloc_cu_ctx[ctx->device] = cur;
   }
   *out = g_noalloc_addr[ctx->device];
   return AEX_OK;

@@ -51,10 +51,9 @@ struct aex_dit {
   float* PRED = nullptr;      // [l_img, in_ch] f32 velocity
   float* LATB = nullptr;      // [l_img, in_ch] f32 Euler ping-pong
   float* TSIN = nullptr;      // [timestep_dim]
-  uint16_t* TSIN16 = nullptr;
-  float* T1 = nullptr;        // [C]
-  uint16_t* T16 = nullptr;    // [C]
+  float* T1 = nullptr;        // [C] time MLP hidden, then silu of it in place
   float* TEMB = nullptr;      // [C]
+  float* TEMBS = nullptr;     // [C] silu(temb), the modulation heads' input
   float* MOD_IMG = nullptr;   // [6C]
   float* MOD_TXT = nullptr;   // [6C]
   float* MOD_SINGLE = nullptr;  // [3C]
@@ -336,9 +335,17 @@ int single_block(aex_dit* d, int i, cudaStream_t s) {
   return AEX_OK;
 }
 
+// An f32-activation GEMV job (the conditioner's f32 qmm, affine_qmm_t_float_gs_64_b_4).
+QmmJob f32_job(const aex_qweight* w, const float* x, int k, float* y, int n) {
+  QmmJob j{w, x, k, 1, y, n, 1, nullptr};
+  j.x_f32 = true;
+  return j;
+}
+
 // Step conditioning from the timestep in CUR[0] (DirectConditioner.stepConditioning,
-// Sources/ImarelloDirect/DirectConditioner.swift:168-213): sinusoid -> time MLP -> SiLU ->
-// modulation vectors of the double (img, txt), single and output layers.
+// Sources/ImarelloDirect/DirectConditioner.swift:168-213), in f32 like the reference's f32 qmm
+// chain: sinusoid -> linear_1 -> SiLU -> linear_2 -> temb -> SiLU -> the modulation vectors of the
+// double (img, txt), single and output layers (the four heads read the same SiLU(temb): one launch).
 int conditioning(aex_dit* d, cudaStream_t s) {
   const int C = d->C, td = d->cfg.timestep_dim;
   AEX_NEED(l1, need_lin(d, "time_guidance_embed.linear_1", C, td));
@@ -348,15 +355,13 @@ int conditioning(aex_dit* d, cudaStream_t s) {
   AEX_NEED(msin, need_lin(d, "single_stream_modulation.linear", 3 * C, C));
   AEX_NEED(mout, need_lin(d, "norm_out.linear", 2 * C, C));
   AEX_TRY(glue::timestep_embedding(d->ctx, d->CUR, td, d->TSIN, s));
-  AEX_TRY(glue::f32_to_bf16(d->ctx, d->TSIN, td, d->TSIN16, s));
-  AEX_TRY(qmm_run(d->ctx, l1, d->TSIN16, td, 1, d->T1, C, 1, nullptr, s));
-  AEX_TRY(glue::silu_to_bf16(d->ctx, d->T1, C, d->T16, s));
-  AEX_TRY(qmm_run(d->ctx, l2, d->T16, C, 1, d->TEMB, C, 1, nullptr, s));
-  AEX_TRY(glue::silu_to_bf16(d->ctx, d->TEMB, C, d->T16, s));
-  AEX_TRY(qmm_run(d->ctx, mimg, d->T16, C, 1, d->MOD_IMG, 6 * C, 1, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, mtxt, d->T16, C, 1, d->MOD_TXT, 6 * C, 1, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, msin, d->T16, C, 1, d->MOD_SINGLE, 3 * C, 1, nullptr, s));
-  AEX_TRY(qmm_run(d->ctx, mout, d->T16, C, 1, d->MOD_OUT, 2 * C, 1, nullptr, s));
+  AEX_TRY(qmm_run_job(d->ctx, f32_job(l1, d->TSIN, td, d->T1, C), s));
+  AEX_TRY(glue::silu_f32(d->ctx, d->T1, C, d->T1, s));
+  AEX_TRY(qmm_run_job(d->ctx, f32_job(l2, d->T1, C, d->TEMB, C), s));
+  AEX_TRY(glue::silu_f32(d->ctx, d->TEMB, C, d->TEMBS, s));
+  const QmmJob heads[4] = {f32_job(mimg, d->TEMBS, C, d->MOD_IMG, 6 * C), f32_job(mtxt, d->TEMBS, C, d->MOD_TXT, 6 * C),
+                           f32_job(msin, d->TEMBS, C, d->MOD_SINGLE, 3 * C), f32_job(mout, d->TEMBS, C, d->MOD_OUT, 2 * C)};
+  AEX_TRY(qmm_run_gemv_group(d->ctx, heads, 4, s));
   d->timestep_set = true;
   return AEX_OK;
 }
@@ -495,10 +500,9 @@ int aex_dit_create(aex_ctx* ctx, const aex_dit_config* cfg, aex_dit** out) {
   if (!r) r = dalloc(d, &d->PRED, static_cast<size_t>(c.l_img) * c.in_channels);
   if (!r) r = dalloc(d, &d->LATB, static_cast<size_t>(c.l_img) * c.in_channels);
   if (!r) r = dalloc(d, &d->TSIN, static_cast<size_t>(c.timestep_dim));
-  if (!r) r = dalloc(d, &d->TSIN16, static_cast<size_t>(c.timestep_dim));
   if (!r) r = dalloc(d, &d->T1, C);
-  if (!r) r = dalloc(d, &d->T16, C);
   if (!r) r = dalloc(d, &d->TEMB, C);
+  if (!r) r = dalloc(d, &d->TEMBS, C);
   if (!r) r = dalloc(d, &d->MOD_IMG, 6 * C);
   if (!r) r = dalloc(d, &d->MOD_TXT, 6 * C);
   if (!r) r = dalloc(d, &d->MOD_SINGLE, 3 * C);

@@ -13,7 +13,7 @@
 //   euler       lat_out = lat_in + dt * v (Flux2Scheduler.step, Flux2Scheduler.swift:101-109)
 //   timestep    cos/sin sinusoid, flip_sin_to_cos (DirectConditioner.sinusoid,
 //               Sources/ImarelloDirect/DirectConditioner.swift:160-170)
-//   silu, f32 -> bf16, bf16 -> f32 row copies.
+//   silu (f32), f32 -> bf16, bf16 -> f32 row copies.
 #include "dit_internal.h"
 #include "sm100.cuh"
 
@@ -116,11 +116,12 @@ __global__ void step_select_kernel(const float* __restrict__ steps, int* counter
   *counter = i + 1;
 }
 
-__global__ void silu_to_bf16_kernel(const float* __restrict__ x, int n, uint16_t* __restrict__ y) {
+// silu in f32 (dd_silu_f32, DirectDiTKernels.swift:175-184; DirectConditioner.silu :135-149).
+__global__ void silu_f32_kernel(const float* __restrict__ x, int n, float* __restrict__ y) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
     const float v = x[i];
-    y[i] = static_cast<uint16_t>(pack_bf16x2(v / (1.f + expf(-v)), 0.f) & 0xFFFFu);
+    y[i] = v / (1.f + expf(-v));
   }
 }
 
@@ -181,9 +182,9 @@ int step_select(aex_ctx* ctx, const float* steps, int* counter, float* cur, cuda
   return check_launch(ctx, "step_select_kernel");
 }
 
-int silu_to_bf16(aex_ctx* ctx, const float* x, int n, void* y, cudaStream_t s) {
-  silu_to_bf16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, n, static_cast<uint16_t*>(y));
-  return check_launch(ctx, "silu_to_bf16_kernel");
+int silu_f32(aex_ctx* ctx, const float* x, int n, float* y, cudaStream_t s) {
+  silu_f32_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, n, y);
+  return check_launch(ctx, "silu_f32_kernel");
 }
 
 int f32_to_bf16(aex_ctx* ctx, const float* x, int64_t n, void* y, cudaStream_t s) {

@@ -21,7 +21,8 @@ int timestep_embedding(aex_ctx* ctx, const float* t_dev, int dim, float* out, cu
 int set_scalar(aex_ctx* ctx, float* dst, float v, cudaStream_t s);
 // cur[0..1] = steps[2i .. 2i+1], i = (*counter)++.
 int step_select(aex_ctx* ctx, const float* steps, int* counter, float* cur, cudaStream_t s);
-int silu_to_bf16(aex_ctx* ctx, const float* x, int n, void* y, cudaStream_t s);
+// y = silu(x) = x / (1 + exp(-x)), f32 (y may equal x).
+int silu_f32(aex_ctx* ctx, const float* x, int n, float* y, cudaStream_t s);
 int f32_to_bf16(aex_ctx* ctx, const float* x, int64_t n, void* y, cudaStream_t s);
 int bf16_to_f32_rows(aex_ctx* ctx, const void* x, int64_t ldx, int rows, int cols, float* y, int64_t ldy,
                      cudaStream_t s);

@@ -97,8 +97,13 @@ struct QmmJob {
   float eps = 0.f;
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  // x is f32 instead of bf16 (GEMV path only: m <= 16).
+  bool x_f32 = false;
 };
 int qmm_run_job(aex_ctx* ctx, const QmmJob& j, cudaStream_t s);
+// One GEMV launch over up to 4 jobs that share x (pointer, pitch, dtype), m <= 16 and k
+// (the conditioning's modulation heads).
+int qmm_run_gemv_group(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s);
 int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s);
 // A copy of `src` (n = plain_rows + 2 * mlp rows: plain rows, then gate rows,
 // then up rows) whose tiles after the plain ones each hold 128 gate rows then
@@ -123,6 +128,13 @@ int launch_attention_core(aex_ctx* ctx, const void* q, const int64_t qs[3], cons
                           const void* v, const int64_t* vs, void* o, const int64_t* os, int B, int S, int S_kv, int H,
                           float scale, float* lse, int64_t lse_sb, int64_t lse_sh, cudaStream_t stream,
                           int kv_splits = 1);
+namespace ring {
+// out = the k partial outputs ([S][H][128] bf16 each: range r at o + r * o_rs, token stride o_ss, head
+// stride o_sh) weighted by 2^(lse_r - lse), lse = log2 sum_r 2^lse_r (range r's log2-sum-exp at
+// lse[r * lse_rs + h * S + s]), rounded to bf16 at out[s * out_ss + h * out_sh]; k <= 16.
+int merge_splits(aex_ctx* ctx, const void* o, int64_t o_rs, int64_t o_ss, int64_t o_sh, const float* lse,
+                 int64_t lse_rs, int k, int S, int H, void* out, int64_t out_ss, int64_t out_sh, cudaStream_t s);
+}  // namespace ring
 // Key-range count for one attention call of `ctas` CTAs over n_kv key blocks
 // on `sms` SMs: the smallest count that fills whole waves noticeably better
 // than no split (at most 4, every range non-empty), else 1.
@@ -152,8 +164,11 @@ aex_ctx* dit_context(aex_dit* d);
 // and 16-byte-aligned pointers, strides, paired rope tables, eps); AEX_OK or
 // AEX_ERR_INVALID_ARG / AEX_ERR_UNSUPPORTED with the message set.
 int validate_attention_args(aex_ctx* ctx, const aex_attention_args* a);
-// Attention (and prep if args ask for it) on validated args.
+// Attention (and prep if args ask for it) on validated args; kv_splits > 1 splits the keys into that many
+// ranges (partial outputs in the scratch after the prepared Q/K, merged into args->out).
 int joint_attention_impl(aex_ctx* ctx, const aex_attention_args* a, void* scratch, size_t scratch_bytes,
-                         cudaStream_t stream);
+                         cudaStream_t stream, int kv_splits = 1);
+// Key ranges the allocating fused call uses for B x S x H on this device (1: no split).
+int fused_kv_splits(const aex_ctx* ctx, int B, int S, int H);
 
 }  // namespace aex

@@ -718,19 +718,33 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 // and then take the K blocks in order as they land, one weight row each.
 // Partial sums of the cluster's splits are reduced in CTA rank 0 through
 // distributed shared memory (no scratch, no atomics, fixed order).
+// One launch may cover up to kGemvMaxProblems weights that read the same x
+// (the conditioning's modulation heads): the CTAs along x are numbered across
+// the problems, so one launch and one fill/drain serve all of them.
+// x is bf16 or f32 (the reference's f32 conditioning qmm,
+// affine_qmm_t_float_gs_64_b_4, DirectConditioner.swift:48,183-190); it is
+// staged as f32 either way, so the arithmetic is the same.
 constexpr int kGemvRows = 128;
 constexpr int kGemvMaxSplit = 8;   // cluster size along K (portable limit)
 constexpr int kGemvMaxKbps = 8;    // K blocks per CTA
+constexpr int kGemvMaxProblems = 4;
 
-struct GemvParams {
-  const uint16_t* x;  // bf16 [m, ldx]
-  int64_t ldx;
+struct GemvProblem {
   const uint8_t* tiles;
-  int m, n, k_blocks, kb_per_split;
+  int n;
+  int cta0;  // first blockIdx.x of this problem
   void* y;
   int64_t ldy;
   int mode;
   const float* gate;
+};
+
+struct GemvParams {
+  const void* x;  // bf16 or f32 [m, ldx]
+  int64_t ldx;
+  int m, k_blocks, kb_per_split;
+  int n_prob;
+  GemvProblem prob[kGemvMaxProblems];
   int* status;
 };
 
@@ -741,8 +755,8 @@ __host__ __device__ constexpr size_t gemv_smem_bytes(int R, int kbps) {
          + 8 + static_cast<size_t>(kbps) * 8;                                    // align + barriers
 }
 
-template <int R>
-__global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
+template <int R, bool XF32>
+__global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t gsm_raw[];
   const int kbps = p.kb_per_split;
   uint8_t* wsm = gsm_raw;
@@ -752,13 +766,19 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(part + R * kGemvRows) + 7) & ~uintptr_t(7));
   __shared__ int abort_flag;
   const int t = threadIdx.x;
+  int pi = 0;
+#pragma unroll
+  for (int i = 1; i < kGemvMaxProblems; ++i)
+    if (i < p.n_prob && static_cast<int>(blockIdx.x) >= p.prob[i].cta0) pi = i;
+  const GemvProblem& q = p.prob[pi];
+  const int cta = static_cast<int>(blockIdx.x) - q.cta0;
   const int split = blockIdx.y;
   const int kb0 = split * kbps;
   const int kb1 = min(p.k_blocks, kb0 + kbps);
   const int nkb = max(0, kb1 - kb0);
-  const int row = blockIdx.x * kGemvRows + t;  // weight row (output column)
-  const int nt = blockIdx.x >> 1, half = blockIdx.x & 1;
-  const bool active = row < p.n;
+  const int row = cta * kGemvRows + t;  // weight row (output column)
+  const int nt = cta >> 1, half = cta & 1;
+  const bool active = row < q.n;
   // 1. Barriers, then every weight copy of this CTA's K range.
   if (t == 0) {
     abort_flag = 0;
@@ -769,37 +789,49 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
   if (t == 0) {
     for (int g = 0; g < nkb; ++g) {
       mbar_arrive_expect_tx(&bars[g], kHalfBytes);
-      bulk_load(wsm + g * kHalfBytes, p.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes, kHalfBytes,
+      bulk_load(wsm + g * kHalfBytes, q.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes, kHalfBytes,
                 &bars[g]);
     }
   }
-  // 2. Stage this split's x slice as f32 (16-byte loads: ldx % 8 == 0 and x 16-byte aligned, checked on
-  //    the host; every load of a thread issued before its stores), then per-group sums.
+  // 2. Stage this split's x slice as f32 (16-byte loads: x 16-byte aligned and its row pitch a multiple of 16
+  //    bytes, checked on the host; every load of a thread issued before its stores), then per-group sums.
   {
-    constexpr int kMaxVec = (R * kGemvMaxKbps * kKB / 8 + kGemvRows - 1) / kGemvRows;
-    const int per_row = nkb * kKB / 8, nvec = R * per_row;
+    constexpr int kPerVec = XF32 ? 4 : 8;  // elements per 16-byte load
+    constexpr int kMaxVec = (R * kGemvMaxKbps * kKB / kPerVec + kGemvRows - 1) / kGemvRows;
+    const int per_row = nkb * kKB / kPerVec, nvec = R * per_row;
     uint4 xv[kMaxVec];
 #pragma unroll
     for (int j = 0; j < kMaxVec; ++j) {
       const int i = t + j * kGemvRows;
       xv[j] = make_uint4(0, 0, 0, 0);
       if (i < nvec) {
-        const int mr = i / per_row, c8 = i % per_row;
-        if (mr < p.m)
-          xv[j] = __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c8);
+        const int mr = i / per_row, c = i % per_row;
+        if (mr < p.m) {
+          if (XF32)
+            xv[j] = __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.x) + static_cast<int64_t>(mr) * p.ldx +
+                                                         kb0 * kKB) + c);
+          else
+            xv[j] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
+                                                         static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
+        }
       }
     }
 #pragma unroll
     for (int j = 0; j < kMaxVec; ++j) {
       const int i = t + j * kGemvRows;
       if (i < nvec) {
-        const int mr = i / per_row, c8 = i % per_row;
-        float* d = xs + mr * kbps * kKB + c8 * 8;
+        const int mr = i / per_row, c = i % per_row;
+        float* d = xs + mr * kbps * kKB + c * kPerVec;
         const uint32_t u[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+        if (XF32) {
+          *reinterpret_cast<float4*>(d) =
+              make_float4(__uint_as_float(u[0]), __uint_as_float(u[1]), __uint_as_float(u[2]), __uint_as_float(u[3]));
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          d[2 * e] = bf16lo_to_f32(u[e]);
-          d[2 * e + 1] = bf16hi_to_f32(u[e]);
+          for (int e = 0; e < 4; ++e) {
+            d[2 * e] = bf16lo_to_f32(u[e]);
+            d[2 * e + 1] = bf16hi_to_f32(u[e]);
+          }
         }
       }
     }
@@ -885,12 +917,12 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(GemvParams p) {
       float v = 0.f;
 #pragma unroll
       for (int c = 0; c < kGemvMaxSplit; ++c) v += pv[c];
-      if (p.mode == kOutResidualGate)
-        static_cast<float*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] += p.gate[row] * v;
-      else if (p.mode == kOutF32)
-        static_cast<float*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] = v;
+      if (q.mode == kOutResidualGate)
+        static_cast<float*>(q.y)[static_cast<int64_t>(mr) * q.ldy + row] += q.gate[row] * v;
+      else if (q.mode == kOutF32)
+        static_cast<float*>(q.y)[static_cast<int64_t>(mr) * q.ldy + row] = v;
       else
-        static_cast<uint16_t*>(p.y)[static_cast<int64_t>(mr) * p.ldy + row] =
+        static_cast<uint16_t*>(q.y)[static_cast<int64_t>(mr) * q.ldy + row] =
             static_cast<uint16_t>(pack_bf16x2(v, 0.f) & 0xFFFFu);
     }
   }
@@ -914,28 +946,48 @@ int validate_q(aex_ctx* ctx, const void* packed, const void* scales, const void*
   return AEX_OK;
 }
 
-template <int R>
-int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
-                int mode, const float* gate, cudaStream_t s) {
-  const int n_ctas = (w->n + qmm::kGemvRows - 1) / qmm::kGemvRows;
+// One GEMV launch over jobs[0, n) (n <= kGemvMaxProblems), which share x, its
+// pitch and dtype, m and k; every job's rows get their own CTAs along x.
+template <int R, bool XF32>
+int launch_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
+  const aex_qweight* w0 = jobs[0].w;
+  qmm::GemvParams p{};
+  p.x = jobs[0].x;
+  p.ldx = jobs[0].ldx;
+  p.m = jobs[0].m;
+  p.k_blocks = w0->k_blocks;
+  p.n_prob = n;
+  p.status = ctx->d_status;
+  int n_ctas = 0;
+  for (int i = 0; i < n; ++i) {
+    const QmmJob& j = jobs[i];
+    qmm::GemvProblem& q = p.prob[i];
+    q.tiles = j.w->tiles;
+    q.n = j.w->n;
+    q.cta0 = n_ctas;
+    q.y = j.y;
+    q.ldy = j.ldy;
+    q.mode = j.mode;
+    q.gate = j.gate;
+    n_ctas += (j.w->n + qmm::kGemvRows - 1) / qmm::kGemvRows;
+  }
   // Enough CTAs to cover every SM several times, and at most kGemvMaxKbps K blocks per CTA.
   int split = std::max(1, std::min(qmm::kGemvMaxSplit, (4 * ctx->sm_count + n_ctas - 1) / n_ctas));
-  split = std::max(split, (w->k_blocks + qmm::kGemvMaxKbps - 1) / qmm::kGemvMaxKbps);
+  split = std::max(split, (w0->k_blocks + qmm::kGemvMaxKbps - 1) / qmm::kGemvMaxKbps);
   if (split > qmm::kGemvMaxSplit)
-    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d needs more than %d K splits", w->k,
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d needs more than %d K splits", w0->k,
                      qmm::kGemvMaxSplit);
-  split = std::min(split, w->k_blocks);
-  int kbps = (w->k_blocks + split - 1) / split;
+  split = std::min(split, w0->k_blocks);
+  const int kbps = (w0->k_blocks + split - 1) / split;
   // x slice + group sums + partials in dynamic shared memory (<= 200 KB).
   auto smem_for = [&](int kb) { return qmm::gemv_smem_bytes(R, kb); };
   constexpr size_t kMaxSmem = 200 * 1024;
   if (smem_for(kbps) > kMaxSmem)
-    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w->k, R);
-  split = (w->k_blocks + kbps - 1) / kbps;
-  AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(qmm::gemv_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kMaxSmem)));
-  qmm::GemvParams p{static_cast<const uint16_t*>(x), ldx, w->tiles, m, w->n, w->k_blocks, kbps, y, ldy, mode, gate,
-                    ctx->d_status};
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w0->k, R);
+  split = (w0->k_blocks + kbps - 1) / kbps;
+  p.kb_per_split = kbps;
+  auto kern = qmm::gemv_kernel<R, XF32>;
+  AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem)));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(n_ctas, split, 1);
   cfg.blockDim = dim3(qmm::kGemvRows, 1, 1);
@@ -948,8 +1000,22 @@ int launch_gemv(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  AEX_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, qmm::gemv_kernel<R>, p));
+  AEX_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, p));
   return check_launch(ctx, "qmm gemv_kernel");
+}
+
+template <bool XF32>
+int run_gemv_t(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
+  const int m = jobs[0].m;
+  if (m <= 1) return launch_gemv<1, XF32>(ctx, jobs, n, s);
+  if (m <= 2) return launch_gemv<2, XF32>(ctx, jobs, n, s);
+  if (m <= 4) return launch_gemv<4, XF32>(ctx, jobs, n, s);
+  if (m <= 8) return launch_gemv<8, XF32>(ctx, jobs, n, s);
+  return launch_gemv<16, XF32>(ctx, jobs, n, s);
+}
+
+int run_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
+  return jobs[0].x_f32 ? run_gemv_t<true>(ctx, jobs, n, s) : run_gemv_t<false>(ctx, jobs, n, s);
 }
 
 }  // namespace
@@ -1042,21 +1108,16 @@ bool gemv_path(const aex_qweight* w, int m) { return m <= 16 && w->k_blocks <= q
 bool use_gemv(const QmmJob& j) { return gemv_path(j.w, j.m) && j.glu_tile0 >= j.w->n_tiles && j.qk_tiles == 0; }
 
 int run_one(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
-  const aex_qweight* w = j.w;
-  if (use_gemv(j)) {
-    if (j.m <= 1) return launch_gemv<1>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
-    if (j.m <= 2) return launch_gemv<2>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
-    if (j.m <= 4) return launch_gemv<4>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
-    if (j.m <= 8) return launch_gemv<8>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
-    return launch_gemv<16>(ctx, w, j.x, j.ldx, j.m, j.y, j.ldy, j.mode, j.gate, s);
-  }
+  if (use_gemv(j)) return run_gemv(ctx, &j, 1, s);
+  if (j.x_f32) return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm: f32 activations take the GEMV path only (m <= 16)");
   return launch_gemm_pair(ctx, &j, 1, s);
 }
 
 int check_job(aex_ctx* ctx, const QmmJob& j) {
   if (j.m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
-  if ((reinterpret_cast<uintptr_t>(j.x) & 15) || j.ldx % 8 || j.ldx < j.w->k)
-    return set_error(ctx, AEX_ERR_INVALID_ARG, "x must be 16-byte aligned with ldx >= k and ldx %% 8 == 0");
+  if ((reinterpret_cast<uintptr_t>(j.x) & 15) || j.ldx % (j.x_f32 ? 4 : 8) || j.ldx < j.w->k)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "x must be 16-byte aligned with ldx >= k and a row pitch of a multiple "
+                     "of 16 bytes");
   if (j.mode == qmm::kOutResidualGate && !j.gate) return set_error(ctx, AEX_ERR_INVALID_ARG, "gate is NULL");
   if (j.glu_tile0 < j.w->n_tiles && (!j.y2 || (reinterpret_cast<uintptr_t>(j.y2) & 15) || j.ldy2 % 8))
     return set_error(ctx, AEX_ERR_INVALID_ARG, "glu output must be 16-byte aligned rows");
@@ -1104,6 +1165,19 @@ int qmm_run(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int 
 int qmm_run_job(aex_ctx* ctx, const QmmJob& j, cudaStream_t s) {
   if (int r = check_job(ctx, j)) return r;
   return run_one(ctx, j, s);
+}
+
+int qmm_run_gemv_group(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
+  if (n < 1 || n > qmm::kGemvMaxProblems)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "gemv group: %d jobs (1..%d)", n, qmm::kGemvMaxProblems);
+  for (int i = 0; i < n; ++i) {
+    const QmmJob& j = jobs[i];
+    if (int r = check_job(ctx, j)) return r;
+    if (!use_gemv(j) || j.x != jobs[0].x || j.ldx != jobs[0].ldx || j.m != jobs[0].m || j.w->k != jobs[0].w->k ||
+        j.x_f32 != jobs[0].x_f32)
+      return set_error(ctx, AEX_ERR_INVALID_ARG, "gemv group: jobs must share x, ldx, m <= 16, k and the x dtype");
+  }
+  return run_gemv(ctx, jobs, n, s);
 }
 
 int qmm_run2(aex_ctx* ctx, const QmmJob& a, const QmmJob& b, cudaStream_t s) {
@@ -1193,21 +1267,33 @@ int aex_qweight_dequantize(aex_ctx* ctx, const aex_qweight* w, uint16_t* out, ae
   return check_launch(ctx, "dequant_tiles_kernel");
 }
 
-int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
-            int y_dtype, aex_stream stream) {
+int aex_qmm_ex(aex_ctx* ctx, const aex_qweight* w, const void* x, int x_dtype, int64_t ldx, int m, void* y,
+               int64_t ldy, int y_dtype, aex_stream stream) {
   using namespace aex;
   if (!ctx || !w || !x || !y) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL argument");
   if (m <= 0) return set_error(ctx, AEX_ERR_INVALID_ARG, "m must be positive");
+  if (x_dtype != AEX_DTYPE_BF16 && x_dtype != AEX_DTYPE_F32)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "x_dtype must be AEX_DTYPE_BF16 or AEX_DTYPE_F32");
   if (y_dtype != AEX_DTYPE_BF16 && y_dtype != AEX_DTYPE_F32)
     return set_error(ctx, AEX_ERR_INVALID_ARG, "y_dtype must be AEX_DTYPE_BF16 or AEX_DTYPE_F32");
-  if (ldx < w->k || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15))
-    return set_error(ctx, AEX_ERR_INVALID_ARG, "x must be 16-byte aligned with ldx >= k and ldx %% 8 == 0");
+  const bool xf32 = x_dtype == AEX_DTYPE_F32;
+  if (ldx < w->k || ldx % (xf32 ? 4 : 8) || (reinterpret_cast<uintptr_t>(x) & 15))
+    return set_error(ctx, AEX_ERR_INVALID_ARG,
+                     "x must be 16-byte aligned with ldx >= k and a row pitch of a multiple of 16 bytes");
   if (ldy < w->n || (reinterpret_cast<uintptr_t>(y) & (y_dtype == AEX_DTYPE_F32 ? 3 : 1)))
     return set_error(ctx, AEX_ERR_INVALID_ARG, "y must be aligned to its element size with ldy >= n");
+  if (xf32 && m > 16)
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "f32 activations are supported for m <= 16 (the conditioning GEMV)");
   if (ctx->device != w->device) return set_error(ctx, AEX_ERR_INVALID_ARG, "weight lives on another device");
   if (int r = bind_device(ctx)) return r;
-  return qmm_run(ctx, w, x, ldx, m, y, ldy, y_dtype == AEX_DTYPE_F32 ? qmm::kOutF32 : qmm::kOutBf16, nullptr,
-                 static_cast<cudaStream_t>(stream));
+  QmmJob j{w, x, ldx, m, y, ldy, y_dtype == AEX_DTYPE_F32 ? qmm::kOutF32 : qmm::kOutBf16, nullptr};
+  j.x_f32 = xf32;
+  return qmm_run_job(ctx, j, static_cast<cudaStream_t>(stream));
+}
+
+int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
+            int y_dtype, aex_stream stream) {
+  return aex_qmm_ex(ctx, w, x, AEX_DTYPE_BF16, ldx, m, y, ldy, y_dtype, stream);
 }
 
 }  // extern "C"

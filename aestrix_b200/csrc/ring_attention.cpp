@@ -7,7 +7,10 @@
 // sequence is split into P equal contiguous shards (rank r holds tokens
 // [r*S_r, (r+1)*S_r), text rows in shard 0). Each rank RMS-normalizes and
 // rotates its own Q and K rows (RoPE uses absolute positions, so rotating
-// before the exchange is exact). Two schedules, the same on every rank:
+// before the exchange is exact). Three schedules, the same on every rank:
+//  * overlap: P - 1 pairwise NCCL groups on a high-priority stream; each
+//    shard's attention starts as soon as it has landed (the local one at
+//    once), one partial per shard, merged by log-sum-exp at the end;
 //  * ring: for hop h = 0..P-1 attend the local queries to the K/V shard of rank
 //    (r - h) mod P while the next shard travels around the ring (ncclSend to
 //    r+1 / ncclRecv from r-1 on a dedicated stream, double buffered); partial
@@ -22,6 +25,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
@@ -35,11 +39,6 @@ namespace ring {
 int merge(aex_ctx* ctx, const void* o_h, int64_t oh_ss, int64_t oh_sh, const float* lse_h, const float* lse_in,
           float* lse_out, float* o_acc, int S, int H, bool first, bool final, void* out, int64_t out_ss, int64_t out_sh,
           cudaStream_t s);
-// out = the k key ranges' partial outputs o[r] ([k][S][H][128] bf16, range
-// stride S*H*128) weighted by 2^(lse[r] - lse), lse = log2 sum_r 2^lse[r]
-// (lse: [k][H][S] f32), rounded to bf16 at out[s*out_ss + h*out_sh].
-int merge_splits(aex_ctx* ctx, const void* o, const float* lse, int k, int S, int H, void* out, int64_t out_ss,
-                 int64_t out_sh, cudaStream_t s);
 }
 
 namespace {
@@ -107,21 +106,35 @@ int group_end(aex_ctx* ctx, ncclComm_t comm, ncclResult_t issued, const char* wh
 }
 
 // Schedule of the sequence-parallel attention, the same on every rank (it
-// depends only on the shapes, equal on all ranks): one all-gather of K/V and
-// one attention call over all keys measured faster than the ring at every P
-// tried (2048^2, P = 2: 1.74 vs 1.81 ms per call), so it is the default while
-// the gathered K and V fit in kGatherMaxBytes; longer sequences take the ring,
-// whose memory per rank stays O(S). AEX_SP_SCHEDULE=ring or =gather overrides.
+// depends only on the shapes, equal on all ranks):
+//  * overlap (default for P > 1 while the gathered K and V fit in
+//    kGatherMaxBytes): the K/V exchange as P - 1 pairwise NCCL groups on a
+//    high-priority stream, the attention over each shard launched as soon as
+//    that shard has landed (the local shard at once), partials merged by
+//    log-sum-exp;
+//  * gather (default at P = 1): one grouped all-gather of K/V, then one
+//    attention call over all keys (measured faster than the ring at every P
+//    tried: 2048^2, P = 2: 1.74 vs 1.81 ms per call; P = 8: 0.747 vs 2.78 ms);
+//  * ring (when the gathered K/V would not fit): K/V passed to rank r + 1 per
+//    hop, memory per rank O(S).
+// AEX_SP_SCHEDULE=overlap|gather|ring overrides.
 constexpr size_t kGatherMaxBytes = size_t{8} << 30;
+constexpr int kMaxOverlapRanks = 16;  // partials merged in one pass (merge_splits)
+enum Schedule : int { kRing = 0, kGather = 1, kOverlap = 2 };
 
-bool use_gather(int P, size_t plane_bytes) {
+int schedule_for(int P, size_t plane_bytes) {
   static const int forced = [] {
     const char* e = getenv("AEX_SP_SCHEDULE");
     if (!e) return -1;
-    return !strcmp(e, "gather") ? 1 : !strcmp(e, "ring") ? 0 : -1;
+    return !strcmp(e, "overlap") ? static_cast<int>(kOverlap)
+           : !strcmp(e, "gather") ? static_cast<int>(kGather)
+           : !strcmp(e, "ring")   ? static_cast<int>(kRing)
+                                  : -1;
   }();
-  if (forced >= 0) return forced == 1;
-  return 2 * static_cast<size_t>(P) * plane_bytes <= kGatherMaxBytes;
+  if (forced == kRing || forced == kGather) return forced;
+  if (forced == kOverlap && P <= kMaxOverlapRanks) return kOverlap;
+  if (2 * static_cast<size_t>(P) * plane_bytes > kGatherMaxBytes) return kRing;
+  return (P > 1 && P <= kMaxOverlapRanks) ? kOverlap : kGather;
 }
 
 }  // namespace
@@ -131,8 +144,10 @@ struct aex_comm {
   aex_ctx* ctx = nullptr;
   ncclComm_t comm = nullptr;
   int world = 0, rank = 0;
-  cudaStream_t stream = nullptr;  // exchange stream
-  cudaEvent_t ev_attn[2] = {nullptr, nullptr}, ev_recv = nullptr, ev_start = nullptr;
+  cudaStream_t stream = nullptr;  // exchange stream (highest priority: its copies take SMs as they free up)
+  cudaStream_t side = nullptr;    // second compute stream of the overlap schedule
+  cudaEvent_t ev_attn[2] = {nullptr, nullptr}, ev_recv = nullptr, ev_start = nullptr, ev_side = nullptr;
+  cudaEvent_t ev_piece[aex::kMaxOverlapRanks] = {};  // overlap schedule: exchange group h has landed
   // exchange state (ring or gather layout), grown on demand
   void* buf = nullptr;
   size_t buf_bytes = 0;
@@ -180,14 +195,34 @@ int key_ranges(int P, int S, int H, int sms) {
 
 int gather_splits(const aex_ctx* ctx, int P, int S, int H) { return key_ranges(P, S, H, ctx->sm_count); }
 
+// The overlap schedule's plan for `rank` of `world` (host logic shared by the CUDA path and the
+// CPU tests): the local shard's attention first (no exchange), then the P - 1 pairwise exchange
+// groups (group h: this rank's K/V to rank r + h, rank r - h's K/V into its slot; a permutation,
+// so the groups pair up on every rank in the same order), then per landed shard one attention
+// into its own partial (alternating two compute streams), then one merge of the P partials.
+int overlap_plan(int P, int r, aex_sp_op* ops, int max_ops) {
+  if (P < 1 || r < 0 || r >= P || P > kMaxOverlapRanks) return -1;
+  const int n = 1 + 2 * (P - 1) + 1;
+  if (!ops) return n;
+  if (max_ops < n) return -1;
+  int i = 0;
+  ops[i++] = aex_sp_op{AEX_SP_OP_ATTEND, -1, -1, r, 0, -1, 0};
+  for (int h = 1; h < P; ++h) ops[i++] = aex_sp_op{AEX_SP_OP_EXCHANGE, (r + h) % P, (r - h + P) % P, -1, h, -1, -1};
+  for (int h = 1; h < P; ++h) ops[i++] = aex_sp_op{AEX_SP_OP_ATTEND, -1, -1, (r - h + P) % P, h, h, h & 1};
+  ops[i++] = aex_sp_op{AEX_SP_OP_MERGE, -1, -1, -1, P, -1, 0};
+  return i;
+}
+
 int sp_buffers(aex_ctx* ctx, aex_comm* c, int S, int H, SpSlots* out) {
   if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
   const int P = c->world, r = c->rank;
   const size_t plane = static_cast<size_t>(H) * S * 128;
   if (align256(plane * 2) != plane * 2) return set_error(ctx, AEX_ERR_INVALID_ARG, "shard size must keep 256-byte alignment");
   uint8_t* base;
-  if (use_gather(P, plane * 2)) {
-    const size_t k = static_cast<size_t>(gather_splits(ctx, P, S, H));
+  const int sched = schedule_for(P, plane * 2);
+  if (sched != kRing) {
+    // gather / overlap layout; the overlap schedule keeps one partial per shard
+    const size_t k = sched == kOverlap ? static_cast<size_t>(P) : static_cast<size_t>(gather_splits(ctx, P, S, H));
     const size_t parts = k > 1 ? k * plane * 2 + align256(k * H * static_cast<size_t>(S) * 4) : 0;
     if (int e = grow(c, plane * 2 * (1 + 2 * static_cast<size_t>(P)) + parts)) return e;
     base = static_cast<uint8_t*>(c->buf);
@@ -301,7 +336,68 @@ int gather_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, 
   if (int e = launch_attention_core(ctx, Q, q_st, Kall, kv_st, Vall, kv_st, parts, p_st, 1, S, P * S, H, scale, lse,
                                     static_cast<int64_t>(H) * S, S, s, k))
     return e;
-  return ring::merge_splits(ctx, parts, lse, k, S, H, out, out_ss, out_sh, s);
+  return ring::merge_splits(ctx, parts, static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128, lse,
+                            static_cast<int64_t>(H) * S, k, S, H, out, out_ss, out_sh, s);
+}
+
+// The overlap schedule (gather layout with P partials): runs overlap_plan. Exchange groups go to the
+// high-priority exchange stream, each recording ev_piece[h] once its shard has landed; an attention over
+// shard h waits for that event on its compute stream (the caller's stream or the side stream), so it starts
+// while later shards are still in flight and the two streams' launches fill each other's tail waves.
+int overlap_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
+                cudaStream_t s) {
+  const int P = c->world, r = c->rank;
+  const size_t plane = static_cast<size_t>(H) * S * 128;
+  uint8_t* base = static_cast<uint8_t*>(c->buf);
+  uint16_t* Q = reinterpret_cast<uint16_t*>(base);
+  uint16_t* Kall = reinterpret_cast<uint16_t*>(base + plane * 2);
+  uint16_t* Vall = reinterpret_cast<uint16_t*>(base + plane * 2 * (1 + static_cast<size_t>(P)));
+  uint16_t* parts = reinterpret_cast<uint16_t*>(base + plane * 2 * (1 + 2 * static_cast<size_t>(P)));
+  float* lse = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(parts) + static_cast<size_t>(P) * plane * 2);
+  aex_sp_op ops[2 * kMaxOverlapRanks + 2];
+  const int n_ops = overlap_plan(P, r, ops, 2 * kMaxOverlapRanks + 2);
+  if (n_ops < 0) return set_error(ctx, AEX_ERR_UNSUPPORTED, "overlap schedule: %d ranks", P);
+  // Q, K, V of this rank were written on s: the exchange and the side stream start after them.
+  AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_start, s));
+  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->stream, c->ev_start, 0));
+  AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(c->side, c->ev_start, 0));
+  const size_t bytes = plane * 2;
+  const int64_t q_st[3] = {static_cast<int64_t>(plane), 128, static_cast<int64_t>(S) * 128};  // head-major
+  const int64_t kv_st[3] = {static_cast<int64_t>(P) * static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128,
+                            128};  // token-major slot of one rank
+  const int64_t p_st[3] = {static_cast<int64_t>(plane), static_cast<int64_t>(H) * 128, 128};
+  for (int i = 0; i < n_ops; ++i) {
+    const aex_sp_op& op = ops[i];
+    if (op.kind == AEX_SP_OP_EXCHANGE) {
+      ncclResult_t nr = nccl().groupStart();
+      if (nr == ncclSuccess)
+        nr = nccl().send(reinterpret_cast<uint8_t*>(Kall) + r * bytes, bytes, ncclChar, op.send_to, c->comm, c->stream);
+      if (nr == ncclSuccess)
+        nr = nccl().send(reinterpret_cast<uint8_t*>(Vall) + r * bytes, bytes, ncclChar, op.send_to, c->comm, c->stream);
+      if (nr == ncclSuccess)
+        nr = nccl().recv(reinterpret_cast<uint8_t*>(Kall) + op.recv_from * bytes, bytes, ncclChar, op.recv_from,
+                         c->comm, c->stream);
+      if (nr == ncclSuccess)
+        nr = nccl().recv(reinterpret_cast<uint8_t*>(Vall) + op.recv_from * bytes, bytes, ncclChar, op.recv_from,
+                         c->comm, c->stream);
+      if (int e = group_end(ctx, c->comm, nr, "ncclSend/ncclRecv (overlap)")) return e;
+      AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_piece[op.part], c->stream));
+    } else if (op.kind == AEX_SP_OP_ATTEND) {
+      cudaStream_t t = op.stream ? c->side : s;
+      if (op.wait_exchange >= 0) AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(t, c->ev_piece[op.wait_exchange], 0));
+      if (int e = launch_attention_core(ctx, Q, q_st, Kall + op.slot * plane, kv_st, Vall + op.slot * plane, kv_st,
+                                        parts + op.part * plane, p_st, 1, S, S, H, scale,
+                                        lse + static_cast<size_t>(op.part) * H * S, 0, S, t))
+        return e;
+    } else {
+      AEX_CUDA_TRY(ctx, cudaEventRecord(c->ev_side, c->side));
+      AEX_CUDA_TRY(ctx, cudaStreamWaitEvent(s, c->ev_side, 0));
+      if (int e = ring::merge_splits(ctx, parts, static_cast<int64_t>(plane), p_st[1], p_st[2], lse,
+                                     static_cast<int64_t>(H) * S, op.part, S, H, out, out_ss, out_sh, s))
+        return e;
+    }
+  }
+  return AEX_OK;
 }
 
 }  // namespace
@@ -309,9 +405,16 @@ int gather_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, 
 int sp_run(aex_ctx* ctx, aex_comm* c, int S, int H, float scale, void* out, int64_t out_ss, int64_t out_sh,
            cudaStream_t s) {
   if (!c->comm) return set_error(ctx, AEX_ERR_NCCL, "communicator aborted");
-  return use_gather(c->world, static_cast<size_t>(H) * S * 256) ? gather_run(ctx, c, S, H, scale, out, out_ss, out_sh, s)
-                              : ring_run(ctx, c, S, H, scale, out, out_ss, out_sh, s);
+  switch (schedule_for(c->world, static_cast<size_t>(H) * S * 256)) {
+    case kOverlap:
+      return overlap_run(ctx, c, S, H, scale, out, out_ss, out_sh, s);
+    case kGather:
+      return gather_run(ctx, c, S, H, scale, out, out_ss, out_sh, s);
+    default:
+      return ring_run(ctx, c, S, H, scale, out, out_ss, out_sh, s);
+  }
 }
+
 
 }  // namespace aex
 
@@ -363,10 +466,17 @@ int aex_comm_create(aex_ctx* ctx, int world, int rank, const void* id, int timeo
     delete c;
     return nccl_error(ctx, r != ncclSuccess ? r : st, "ncclCommInitRankConfig");
   }
-  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  // The exchange stream at the highest priority: its copy kernels take SMs as attention CTAs retire.
+  int least = 0, greatest = 0;
+  cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&c->stream, cudaStreamNonBlocking, greatest);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
   for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&c->ev_attn[i], cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_recv, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming);
+  for (int i = 0; i < std::min(world, static_cast<int>(kMaxOverlapRanks)) && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&c->ev_piece[i], cudaEventDisableTiming);
   if (e != cudaSuccess) {
     aex_comm_destroy(c);
     return cuda_error(ctx, e, "stream/event creation");
@@ -380,10 +490,14 @@ void aex_comm_destroy(aex_comm* c) {
   if (!c) return;
   cudaSetDevice(c->ctx->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->side) cudaStreamSynchronize(c->side);
   if (c->comm) nccl().commDestroy(c->comm);
-  for (auto* ev : {c->ev_attn[0], c->ev_attn[1], c->ev_recv, c->ev_start})
+  for (auto* ev : {c->ev_attn[0], c->ev_attn[1], c->ev_recv, c->ev_start, c->ev_side})
+    if (ev) cudaEventDestroy(ev);
+  for (auto* ev : c->ev_piece)
     if (ev) cudaEventDestroy(ev);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->side) cudaStreamDestroy(c->side);
   if (c->buf) cudaFree(c->buf);
   delete c;
 }
@@ -403,8 +517,10 @@ int aex_sp_key_ranges(int world, int seq, int heads, int sms) {
 
 int aex_sp_schedule(int world, int seq, int heads) {
   if (world < 1 || seq <= 0 || heads <= 0) return -1;
-  return aex::use_gather(world, static_cast<size_t>(heads) * seq * 256) ? 1 : 0;
+  return aex::schedule_for(world, static_cast<size_t>(heads) * seq * 256);
 }
+
+int aex_sp_plan(int world, int rank, aex_sp_op* ops, int max_ops) { return aex::overlap_plan(world, rank, ops, max_ops); }
 
 int aex_ring_attention(aex_ctx* ctx, aex_comm* c, const aex_attention_args* a, aex_stream stream) {
   using namespace aex;

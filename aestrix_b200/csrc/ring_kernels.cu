@@ -56,32 +56,27 @@ __global__ void merge_kernel(const uint16_t* __restrict__ o_h, int64_t oh_ss, in
   }
 }
 
-// One thread per (token s, head h, 8 columns): all k ranges at once.
-constexpr int kMaxSplits = 4;
-__global__ void merge_splits_kernel(const uint16_t* __restrict__ o, const float* __restrict__ lse, int k, int S,
-                                    int H, uint16_t* __restrict__ out, int64_t out_ss, int64_t out_sh) {
+// One thread per (token s, head h, 8 columns): all k ranges at once. Range r's
+// partial output sits at o + r * o_rs (token stride o_ss, head stride o_sh) and
+// its log2-sum-exp at lse[r * lse_rs + h * S + s].
+constexpr int kMaxSplits = 16;
+__global__ void merge_splits_kernel(const uint16_t* __restrict__ o, int64_t o_rs, int64_t o_ss, int64_t o_sh,
+                                    const float* __restrict__ lse, int64_t lse_rs, int k, int S, int H,
+                                    uint16_t* __restrict__ out, int64_t out_ss, int64_t out_sh) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(S) * H * 16) return;
   const int c = static_cast<int>(idx & 15);
   const int64_t sh = idx >> 4;
   const int h = static_cast<int>(sh % H);
   const int s = static_cast<int>(sh / H);
-  const int64_t plane = static_cast<int64_t>(S) * H * 128;
-  float l[kMaxSplits];
   float mx = -INFINITY;
-#pragma unroll
-  for (int r = 0; r < kMaxSplits; ++r) {
-    l[r] = r < k ? lse[(static_cast<int64_t>(r) * H + h) * S + s] : -INFINITY;
-    mx = fmaxf(mx, l[r]);
-  }
+  for (int r = 0; r < k; ++r) mx = fmaxf(mx, lse[r * lse_rs + static_cast<int64_t>(h) * S + s]);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float wsum = 0.f;
-#pragma unroll
-  for (int r = 0; r < kMaxSplits; ++r) {
-    if (r >= k) break;
-    const float w = exp2f(l[r] - mx);
+  for (int r = 0; r < k; ++r) {
+    const float w = exp2f(lse[r * lse_rs + static_cast<int64_t>(h) * S + s] - mx);
     wsum += w;
-    const uint4 raw = *reinterpret_cast<const uint4*>(o + r * plane + (static_cast<int64_t>(s) * H + h) * 128 + c * 8);
+    const uint4 raw = *reinterpret_cast<const uint4*>(o + r * o_rs + s * o_ss + h * o_sh + c * 8);
     const uint32_t rv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -97,12 +92,13 @@ __global__ void merge_splits_kernel(const uint16_t* __restrict__ o, const float*
 
 }  // namespace
 
-int merge_splits(aex_ctx* ctx, const void* o, const float* lse, int k, int S, int H, void* out, int64_t out_ss,
-                 int64_t out_sh, cudaStream_t s) {
-  if (k < 1 || k > kMaxSplits) return set_error(ctx, AEX_ERR_INVALID_ARG, "merge_splits: %d ranges", k);
+int merge_splits(aex_ctx* ctx, const void* o, int64_t o_rs, int64_t o_ss, int64_t o_sh, const float* lse,
+                 int64_t lse_rs, int k, int S, int H, void* out, int64_t out_ss, int64_t out_sh, cudaStream_t s) {
+  if (k < 1 || k > kMaxSplits) return set_error(ctx, AEX_ERR_INVALID_ARG, "merge_splits: %d ranges (1..%d)", k, kMaxSplits);
   const int64_t n = static_cast<int64_t>(S) * H * 16;
   merge_splits_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
-      static_cast<const uint16_t*>(o), lse, k, S, H, static_cast<uint16_t*>(out), out_ss, out_sh);
+      static_cast<const uint16_t*>(o), o_rs, o_ss, o_sh, lse, lse_rs, k, S, H, static_cast<uint16_t*>(out), out_ss,
+      out_sh);
   return check_launch(ctx, "merge_splits_kernel");
 }
 

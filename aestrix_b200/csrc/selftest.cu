@@ -1,4 +1,6 @@
-// selftest.cu — tensor-core bring-up check: one 128 x N x 128 bf16 UMMA with
+// selftest.cu — device self tests. aex_selftest_wait: a bounded wait that is
+// made to run out (failure detection without a GPU fault). aex_selftest_umma:
+// tensor-core bring-up check, one 128 x N x 128 bf16 UMMA with
 // the three operand configurations the attention and qmm kernels rely on:
 //   mode 0: A, B from shared memory, both K-major (S = Q K^T; qmm mainloop)
 //   mode 1: A from tensor memory, B N-major in shared memory (O += P V)
@@ -138,8 +140,43 @@ int launch_selftest(aex_ctx* ctx, const uint16_t* a, const uint16_t* b, float* d
   return check_launch(ctx, "umma_selftest_kernel");
 }
 
+// One warp waits on an mbarrier that nothing arrives on, with the same bounded
+// loop the library's kernels use but a caller-chosen limit: after limit_ns of
+// %globaltimer time it records kDevTimeoutSelftest in the status word and
+// returns. Nothing else is in flight (no copies, no tensor memory), so the
+// kernel ends cleanly and the context stays usable.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t a = smem_u32(&bar);
+  const uint64_t t0 = globaltimer_ns();
+  bool done = false;
+  while (!done) {
+    done = mbar_try_wait(a, 0);
+    if (!done && globaltimer_ns() - t0 > limit_ns) {
+      if (threadIdx.x == 0) atomicCAS(status, 0, kDevTimeoutSelftest);
+      break;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace aex
+
+extern "C" int aex_selftest_wait(aex_ctx* ctx, int timeout_us, aex_stream stream) {
+  using namespace aex;
+  if (!ctx) return set_error(ctx, AEX_ERR_INVALID_ARG, "NULL ctx");
+  if (timeout_us < 1 || timeout_us > 1000000)
+    return set_error(ctx, AEX_ERR_INVALID_ARG, "selftest wait: timeout_us %d outside [1, 1000000]", timeout_us);
+  if (int r = bind_device(ctx)) return r;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(timeout_us) * 1000ull,
+                                                                        ctx->d_status);
+  return check_launch(ctx, "wait_selftest_kernel");
+}
 
 extern "C" int aex_selftest_umma(aex_ctx* ctx, int mode, const uint16_t* a, const uint16_t* b, int n, float* d,
                                  aex_stream stream) {

@@ -30,6 +30,7 @@ enum DevStatus : int {
   kDevTimeoutEpilogue = 4,
   kDevTimeoutProducer = 5,
   kDevBadTmem = 6,
+  kDevTimeoutSelftest = 7,  // aex_selftest_wait: the deliberately unanswered wait ran out
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

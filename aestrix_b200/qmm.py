@@ -81,15 +81,17 @@ class QuantizedWeight:
 
 
 def quantized_mm(x, w: QuantizedWeight, out_dtype=torch.bfloat16, out=None, stream=None):
-    """y[m, n] = x[m, k] . deq(W)[n, k]^T; x bf16 [m, k] (row stride ldx), y bf16 or f32."""
-    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.stride(1) != 1:
-        raise TypeError("x must be a 2-D CUDA bfloat16 tensor with contiguous rows")
+    """y[m, n] = x[m, k] . deq(W)[n, k]^T; x bf16 [m, k] (row stride ldx), or f32 for m <= 16 (the
+    conditioner's f32 qmm, DirectConditioner.swift:48); y bf16 or f32."""
+    if x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda or x.dim() != 2 or x.stride(1) != 1:
+        raise TypeError("x must be a 2-D CUDA bfloat16 or float32 tensor with contiguous rows")
     m = x.shape[0]
     if out is None:
         out = torch.empty(m, w.n, dtype=out_dtype, device=x.device)
     dt = _lib.AEX_DTYPE_F32 if out.dtype == torch.float32 else _lib.AEX_DTYPE_BF16
-    w.ctx.check(_lib.lib().aex_qmm(w.ctx.handle, w.handle, x.data_ptr(), x.stride(0), m, out.data_ptr(),
-                                   out.stride(0), dt, _stream_ptr(stream)))
+    xdt = _lib.AEX_DTYPE_F32 if x.dtype == torch.float32 else _lib.AEX_DTYPE_BF16
+    w.ctx.check(_lib.lib().aex_qmm_ex(w.ctx.handle, w.handle, x.data_ptr(), xdt, x.stride(0), m, out.data_ptr(),
+                                      out.stride(0), dt, _stream_ptr(stream)))
     return out
 
 

@@ -99,38 +99,82 @@ def _rope_tables():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """SM clock / throttle-reason sampling during the timed region: NVML polled every ~2 ms from a
+    thread (so even a few-millisecond timed region gets samples), else `nvidia-smi -lms 100`."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.nvml = None
+        self.stop = False
+        self.samples: list[tuple] = []  # (sm_mhz, max_mhz, power_w, reasons set)
+        self.source = "none"
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop:
+                    try:
+                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        bits = int(reasons_fn(h))
+                        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        rs = {nm for nm, bit in self.REASON_BITS.items() if bits & bit}
+                        self.samples.append((sm, max_mhz, pw, rs))
+                    except Exception:
+                        pass
+                    time.sleep(0.002)
+
+            self.nvml = pynvml
+            self.source = "nvml (2 ms poll)"
+            self.t = threading.Thread(target=poll, daemon=True)
             self.t.start()
-            # NVML initialisation can stall the GPU briefly: let it finish before any timing.
-            t0 = time.time()
-            while not self.lines and time.time() - t0 < 10:
-                time.sleep(0.02)
-            self.n_pre = len(self.lines)
         except Exception:
-            self.proc = None
+            self.nvml = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.source = "nvidia-smi (100 ms)"
+                self.t = threading.Thread(target=self._read, daemon=True)
+                self.t.start()
+            except Exception:
+                self.proc = None
+        # NVML initialisation can stall the GPU briefly: let it finish before any timing.
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 10 and (self.nvml or self.proc):
+            time.sleep(0.02)
+        self.n_pre = len(self.samples)
         return self
 
     def _read(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = [p.strip() for p in line.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx, pw = float(parts[1]), float(parts[2]), float(parts[3])
+            except ValueError:
+                continue
+            self.samples.append((sm, mx, pw, {nm for nm, v in zip(names, parts[5:9]) if v.lower() == "active"}))
 
     def __exit__(self, *a):
+        self.stop = True
         if self.proc:
             self.proc.terminate()
             try:
@@ -139,26 +183,16 @@ class ClockSampler:
                 self.proc.kill()
 
     def mark(self):
-        return len(self.lines)
+        return len(self.samples)
 
-    def summary(self, since: int = 0):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines[since:]:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+    def summary(self, since: int = 0, until: int | None = None):
+        sel = self.samples[since:until]
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0, "source": self.source}
+        reasons = set().union(*(x[3] for x in sel))
+        return {"sm_mhz": statistics.median(x[0] for x in sel), "sm_max_mhz": sel[-1][1],
+                "power_w_max": max(x[2] for x in sel), "reasons": sorted(reasons), "samples": len(sel),
+                "source": self.source}
 
 
 def _dist_init():
@@ -227,9 +261,10 @@ def cpu_baseline_sample(threads: int | None = None, rows: int = SEQ):
 def run_reference(args):
     """Reference arm: the CPU restatement of the reference composition on all host cores.
 
-    One step = the fused norm -> RoPE -> SDPA of one head (its own Q/K norm and RoPE, all
-    4608 keys) for a sample of its query rows; heads rotate over steps. The row count is
-    calibrated during warm-up so that all W + K steps take about --ref-seconds."""
+    One step = the fused norm -> RoPE -> SDPA of the 1024^2 call (all 24 heads, each with its own
+    Q/K RMSNorm and RoPE, all 4608 keys) for `rows` query rows: all 4608 (the whole call) when
+    W + K whole calls fit in --ref-seconds, else the largest row count that does (said in `sample`).
+    `ms_per_step` is the measured time of one such step; `value` = the FLOPs the steps did / time."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -239,37 +274,40 @@ def run_reference(args):
     cores = int(os.environ.get("AEXO_THREADS", os.cpu_count() or 1))
     rng = np.random.default_rng(7)
     q, k, v = (rng.standard_normal((1, SEQ, HEADS, HEAD_DIM), dtype=np.float32) for _ in range(3))
-    heads = [tuple(np.ascontiguousarray(a[:, :, h:h + 1]) for a in (q, k, v)) for h in range(HEADS)]
     wq = (1 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32)
     wk = (1 + 0.1 * rng.standard_normal(HEAD_DIM)).astype(np.float32)
     cos, sin = _rope_tables()
 
-    def ref_step(i, rows):
-        qh, kh, vh = heads[i % HEADS]
-        O.joint_attention(qh, kh, vh, wq, wk, 1e-6, cos, sin, q_begin=0, q_end=rows)
+    def ref_step(rows):
+        O.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, q_begin=0, q_end=rows)
 
     t0 = time.perf_counter()
-    ref_step(0, SEQ)
-    t_full = time.perf_counter() - t0
+    ref_step(256)
+    t_probe = (time.perf_counter() - t0) * SEQ / 256  # estimated whole-call time
     budget = args.ref_seconds / max(1, args.steps + args.warmup)
-    rows = int(min(SEQ, max(64, SEQ * budget / t_full)))
-    for i in range(args.warmup):
-        ref_step(i, rows)
+    rows = SEQ if t_probe <= budget else int(max(256, min(SEQ, SEQ * budget / t_probe)) // 128 * 128)
+    for _ in range(args.warmup):
+        ref_step(rows)
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        ref_step(i, rows)
+    for _ in range(args.steps):
+        ref_step(rows)
     dt = time.perf_counter() - t0
-    flops = 4.0 * rows * SEQ * HEAD_DIM * args.steps
+    flops = 4.0 * rows * SEQ * HEAD_DIM * HEADS * args.steps
     value = flops / dt / 1e12
-    sample = f"per step: 1 of {HEADS} heads (own RMSNorm+RoPE, all {SEQ} keys), {rows} of {SEQ} query rows, fp32"
+    if rows == SEQ:
+        sample = f"per step: the whole call ({HEADS} heads x {SEQ} query rows, own RMSNorm+RoPE, all keys), fp32"
+    else:
+        sample = (f"per step: {rows} of {SEQ} query rows x all {HEADS} heads (own RMSNorm+RoPE, all {SEQ} keys), "
+                  f"fp32; the whole call does not fit {args.steps + args.warmup} steps in --ref-seconds")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": FLOPS_PER_CALL / (value * 1e12) * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": dict(CONFIG, reference="CPU restatement of the reference composition (oracle/aex_oracle.cpp); "
-                       "the reference's own Swift/MLX/Metal path is unavailable on this box"),
+        "config": CONFIG,
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU restatement of the reference composition (oracle/aex_oracle.cpp) on all host cores; the "
+                "reference's own Swift/MLX/Metal path cannot run on this box",
     }
     emit(line)
     return 0
@@ -589,9 +627,8 @@ def run_ours(args):
     clk_end = clk.mark()
     _barrier(world)
     clk.__exit__()
-    clocks = clk.summary(clk_mark) if clk_end > clk_mark else dict(clk.summary(clk.n_pre), note="timed region "
-                                                                   "shorter than the 100 ms sample period: "
-                                                                   "samples from warm-up through timing")
+    clocks = clk.summary(clk_mark, clk_end) if clk_end > clk_mark else dict(
+        clk.summary(clk.n_pre), note="no sample fell inside the timed region: samples from warm-up through timing")
     ms_local = ev0.elapsed_time(ev1) / args.steps
     ms = _max_over_ranks(world, ms_local)
     ctx.sync(stream.cuda_stream)
@@ -718,7 +755,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=SEQ, help="query rows in the CPU-baseline sample")
-    ap.add_argument("--ref-seconds", type=float, default=90.0, help="target duration of the reference arm")
+    ap.add_argument("--ref-seconds", type=float, default=150.0, help="target duration of the reference arm")
     ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 4-step DiT denoise measurement")
     ap.add_argument("--no-ring", action="store_true", help="skip the 2048^2 ring attention and sequence-parallel denoise measurements (N > 1)")

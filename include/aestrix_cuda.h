@@ -141,7 +141,9 @@ int aex_joint_attention_ws(aex_ctx* ctx, const aex_attention_args* args, void* s
  * batch*heads*seq <= 131072 (the 1024^2 call uses 110592). Larger args are
  * rejected with AEX_ERR_INVALID_ARG. The first call on a device resolves the
  * array's device address (cudaGetSymbolAddress) with that device current; make
- * that first call before any stream capture. Every call shares the one array:
+ * that first call before any stream capture. The address is cached per device
+ * together with the CUDA context it was resolved in, and resolved again by the
+ * first call in a new context (after cudaDeviceReset). Every call shares the one array:
  * calls whose executions overlap on the GPU (different streams or contexts of
  * the same device) race on it. Each call fully rewrites the part it reads, so
  * no state from an earlier call leaks into a result. */
@@ -192,6 +194,16 @@ int aex_qweight_dequantize(aex_ctx* ctx, const aex_qweight* w, uint16_t* out, ae
  * qmm dispatch (Sources/ImarelloDirect/DirectDiTStep.swift:374-406). */
 int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int m, void* y, int64_t ldy,
             int y_dtype, aex_stream stream);
+
+/* aex_qmm with the activation dtype chosen: x_dtype AEX_DTYPE_BF16 (as
+ * aex_qmm) or AEX_DTYPE_F32 (row pitch ldx a multiple of 4 elements; m <= 16,
+ * else AEX_ERR_UNSUPPORTED). Reference: the conditioner's f32 qmm
+ * affine_qmm_t_float_gs_64_b_4 on f32 activations (timestep MLP, modulation
+ * heads, norm_out; Sources/ImarelloDirect/DirectConditioner.swift:48,98-116,
+ * 183-190). The dot keeps f32 throughout: y = sum_g scale_g * sum(x * q) +
+ * bias_g * sum(x), the unrounded dequantized weights. */
+int aex_qmm_ex(aex_ctx* ctx, const aex_qweight* w, const void* x, int x_dtype, int64_t ldx, int m, void* y,
+               int64_t ldy, int y_dtype, aex_stream stream);
 
 /* ------------------------------------------------------------ DiT engine */
 
@@ -306,8 +318,28 @@ int aex_comm_abort(aex_comm* comm);
 int aex_ring_attention(aex_ctx* ctx, aex_comm* comm, const aex_attention_args* args, aex_stream stream);
 /* The exchange schedule aex_ring_attention and the sequence-parallel engine take
  * for `world` shards of `seq` tokens x `heads` heads: 0 ring, 1 all-gather,
- * -1 bad arguments. */
+ * 2 overlap (pairwise exchange overlapped with per-shard attention; the
+ * default for world > 1 while the gathered K/V fit in 8 GiB), -1 bad
+ * arguments. AEX_SP_SCHEDULE=overlap|gather|ring overrides. */
 int aex_sp_schedule(int world, int seq, int heads);
+
+/* One step of the overlap schedule's plan (host logic, no GPU needed). */
+#define AEX_SP_OP_EXCHANGE 0 /* one NCCL group: this rank's K/V to send_to, recv_from's K/V into slot recv_from */
+#define AEX_SP_OP_ATTEND 1   /* attention of the local queries over slot `slot` into partial `part` */
+#define AEX_SP_OP_MERGE 2    /* log-sum-exp merge of partials [0, part) into the output */
+typedef struct aex_sp_op {
+  int kind;
+  int send_to, recv_from; /* EXCHANGE */
+  int slot;               /* ATTEND: the rank whose K/V shard it reads */
+  int part;               /* EXCHANGE: its index h (1..world-1); ATTEND: partial index; MERGE: partial count */
+  int wait_exchange;      /* ATTEND: the EXCHANGE index h whose shard it reads, -1 for the local shard */
+  int stream;             /* ATTEND: 0 the caller's stream, 1 the communicator's second compute stream */
+} aex_sp_op;
+/* The overlap schedule's steps for `rank` of `world`, in issue order, into ops
+ * (max_ops entries); returns the step count (ops NULL: just the count), -1 for
+ * bad arguments or world > 16. The same plan drives aex_ring_attention's
+ * overlap schedule. No reference counterpart (the reference is one device). */
+int aex_sp_plan(int world, int rank, aex_sp_op* ops, int max_ops);
 /* Key ranges the all-gather schedule's attention call splits into on a device
  * of `sms` SMs (1: no split; at most 4), chosen so the CTAs of a short shard
  * fill whole waves: 2048^2 at world 8 (2,112 rows, 24 heads) on 148 SMs gives
@@ -338,6 +370,15 @@ int aex_dit_set_sequence_parallel(aex_dit* dit, aex_comm* comm, int l_txt_total,
  * n must be 128 or 256 (256 only for mode 0). Device pointers. */
 int aex_selftest_umma(aex_ctx* ctx, int mode, const uint16_t* a, const uint16_t* b, int n, float* d,
                       aex_stream stream);
+
+/* Failure-detection self test (no reference counterpart; the analogue of the
+ * reference's command-buffer error check after waitUntilCompleted,
+ * DirectDiTStep.swift:968-970): launches one kernel that waits on a barrier
+ * nothing arrives on, bounded by timeout_us (1 .. 1e6) of device time instead
+ * of the library's 2 s, after which it records a device status and returns
+ * without faulting. The next aex_sync on `stream` then returns AEX_ERR_DEVICE
+ * (and clears the status); the context stays usable. */
+int aex_selftest_wait(aex_ctx* ctx, int timeout_us, aex_stream stream);
 
 #ifdef __cplusplus
 }

@@ -108,18 +108,30 @@ void aexo_pack_q4(const uint8_t* codes, int n, int k, uint32_t* packed) {
 
 void aexo_qmm(const float* x, int m, const uint32_t* packed, const uint16_t* scales, const uint16_t* biases,
               int n, int k, int group_size, float* y) {
-  parallel_for(n, 16, [&](int64_t r) {
+  // Blocks of kRows weight rows: each block is dequantized once, then every x
+  // row is read once per block (not once per weight row). The f64 dot products
+  // are vectorized (a fixed lane order: deterministic for a given build).
+  constexpr int kRows = 16;
+  const int64_t blocks = (n + kRows - 1) / kRows;
+  parallel_for(blocks, 1, [&](int64_t blk) {
+    const int r0 = static_cast<int>(blk * kRows);
+    const int nr = std::min(kRows, n - r0);
     std::vector<uint16_t> wrow_bf(k);
-    std::vector<float> wrow(k);
-    {
-      dequant_row(packed + (size_t)r * (k / 8), scales + (size_t)r * (k / group_size),
-                  biases + (size_t)r * (k / group_size), k, group_size, wrow_bf.data());
-      for (int c = 0; c < k; ++c) wrow[c] = aexo_bf16_to_f32(wrow_bf[c]);
-      for (int i = 0; i < m; ++i) {
-        const float* xi = x + (size_t)i * k;
+    std::vector<float> wblk(static_cast<size_t>(nr) * k);
+    for (int j = 0; j < nr; ++j) {
+      const size_t r = static_cast<size_t>(r0 + j);
+      dequant_row(packed + r * (k / 8), scales + r * (k / group_size), biases + r * (k / group_size), k, group_size,
+                  wrow_bf.data());
+      for (int c = 0; c < k; ++c) wblk[(size_t)j * k + c] = aexo_bf16_to_f32(wrow_bf[c]);
+    }
+    for (int i = 0; i < m; ++i) {
+      const float* xi = x + (size_t)i * k;
+      for (int j = 0; j < nr; ++j) {
+        const float* w = wblk.data() + (size_t)j * k;
         double acc = 0.0;
-        for (int c = 0; c < k; ++c) acc += (double)xi[c] * (double)wrow[c];
-        y[(size_t)i * n + r] = static_cast<float>(acc);
+#pragma omp simd reduction(+ : acc)
+        for (int c = 0; c < k; ++c) acc += (double)xi[c] * (double)w[c];
+        y[(size_t)i * n + r0 + j] = static_cast<float>(acc);
       }
     }
   });

@@ -6,23 +6,20 @@ fixed 64 MiB array inside the library.
 
 Checked through the C ABI against the allocating entry point aex_joint_attention
 on two calls in a row (different inputs and shapes, so the second call runs on
-scratch still holding the first call's data), with the attention tolerance of
-the other tests: relative L2 <= 1e-2 and max-abs <= 2e-2. This file is named to
-be collected last, so a run that stops at the first failure has already run
-every other test.
+scratch still holding the first call's data). Both entry points run the same
+kernels on the same inputs, so their outputs must be equal bit for bit: any
+difference (a stale-scratch read, a wrong scratch address) fails the test,
+which a tolerance could hide. This file is named to be collected last, so a
+run that stops at the first failure has already run every other test.
 """
 import ctypes as C
 
-import numpy as np
 import pytest
 import torch
 
 from aestrix_b200 import _lib, attention
 
 pytestmark = pytest.mark.gpu
-
-REL_TOL = 1e-2
-ABS_TOL = 2e-2
 
 
 def _case(seed, b, s, h):
@@ -43,7 +40,7 @@ def _call(ctx, fn, case, out):
 def test_noalloc_matches_allocating_entry_point_twice(cuda_ctx):
     L = _lib.lib()
     cases = [_case(901, 1, 4608, 24), _case(902, 2, 700, 8)]  # the 1024^2 call, then a ragged batched one
-    outs_na = [torch.empty_like(c[0]) for c in cases]
+    outs_na = [torch.full_like(c[0], float("nan")) for c in cases]
     for c, o in zip(cases, outs_na):  # two no-alloc calls in a row
         _call(cuda_ctx, L.aex_joint_attention_noalloc, c, o)
     cuda_ctx.sync()
@@ -51,19 +48,17 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda_ctx):
         o_ref = torch.empty_like(c[0])
         _call(cuda_ctx, L.aex_joint_attention, c, o_ref)
         cuda_ctx.sync()
-        got, ref = o_na.float().cpu().numpy(), o_ref.float().cpu().numpy()
-        assert np.isfinite(got).all()
-        rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
-        mx = float(np.abs(got - ref).max())
-        assert rel <= REL_TOL and mx <= ABS_TOL, f"rel-L2 {rel:.3e} max-abs {mx:.3e}"
+        assert torch.isfinite(o_na.float()).all()
+        assert torch.equal(o_na, o_ref), "no-alloc output differs from aex_joint_attention's"
     assert cuda_ctx.device_status() == 0
 
 
 def test_noalloc_rejects_args_beyond_its_scratch(cuda_ctx):
-    q, k, v, wq, wk, cos, sin = _case(903, 1, 64, 4)
+    """2 x 4608 x 24 = 221184 rows > 131072: rejected before any launch. The tensors have the
+    claimed shape, so even a regressed size check would launch on valid memory, not fault."""
+    q, k, v, wq, wk, cos, sin = _case(903, 2, 4608, 24)
     out = torch.empty_like(q)
     a = attention.make_args(q, k, v, out, "bshd", wq, wk, 1e-5, cos, sin)
-    a.batch, a.seq, a.heads = 2, 4608, 24  # 221184 rows > 131072: rejected before any launch
     rc = _lib.lib().aex_joint_attention_noalloc(cuda_ctx.handle, C.byref(a), None)
     assert rc == _lib.AEX_ERR_INVALID_ARG
     assert b"fixed" in _lib.lib().aex_last_error_string(cuda_ctx.handle)
