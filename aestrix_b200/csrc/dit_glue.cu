@@ -41,27 +41,54 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return red[0];
 }
 
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (w == 0) {
+    t = l < (blockDim.x >> 5) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (l == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
 // One CTA per row; C a multiple of 4. Two-pass (mean, then centered variance)
-// in f32 from registers/L1.
+// in f32 from registers/L1. A row whose magnitude exceeds 2^48 (where the sum
+// of C squares could pass the f32 range; the residual stream of a deep stack
+// can grow that large) takes its variance on x scaled by an exact power of two
+// 2^-e, so the result is the one an unbounded-range f32 computation would
+// give; other rows compute exactly as without the scaling.
 __global__ void __launch_bounds__(kRowThreads) ln_mod_kernel(const float* __restrict__ x, int64_t ldx, int C,
                                                              const float* __restrict__ scale,
                                                              const float* __restrict__ shift, float eps,
                                                              __nv_bfloat16* __restrict__ y, int64_t ldy) {
   __shared__ float red[32];
   const float* xr = x + static_cast<int64_t>(blockIdx.x) * ldx;
-  float s = 0.f;
+  float s = 0.f, amax = 0.f;
   for (int i = threadIdx.x * 4; i < C; i += kRowThreads * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);
     s += (v.x + v.y) + (v.z + v.w);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
   const float mean = block_sum(s, red) / C;
+  amax = block_max(amax, red);
+  // 2^-e with 2^e the power of two at or below amax, when amax > 2^48 (else 1)
+  const float sc = (amax > 281474976710656.0f && amax <= 3.4028235e38f) ? __uint_as_float((254u - ((__float_as_uint(amax) >> 23) & 0xFFu)) << 23)
+                                             : 1.0f;
   float q = 0.f;
   for (int i = threadIdx.x * 4; i < C; i += kRowThreads * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);
-    const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
+    const float a = (v.x - mean) * sc, b = (v.y - mean) * sc, c = (v.z - mean) * sc, d = (v.w - mean) * sc;
     q += (a * a + b * b) + (c * c + d * d);
   }
-  const float inv = rsqrtf(block_sum(q, red) / C + eps);
+  const float inv = rsqrtf(block_sum(q, red) / C + eps * sc * sc) * sc;
   __nv_bfloat16* yr = y + static_cast<int64_t>(blockIdx.x) * ldy;
   for (int i = threadIdx.x * 4; i < C; i += kRowThreads * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);

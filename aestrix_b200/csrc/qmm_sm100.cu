@@ -726,7 +726,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 // staged as f32 either way, so the arithmetic is the same.
 constexpr int kGemvRows = 128;
 constexpr int kGemvMaxSplit = 8;   // cluster size along K (portable limit)
-constexpr int kGemvMaxKbps = 8;    // K blocks per CTA
+constexpr int kGemvMaxKbps = 16;   // K blocks per CTA
 constexpr int kGemvMaxProblems = 4;
 
 struct GemvProblem {
@@ -797,32 +797,35 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
   //    bytes, checked on the host; every load of a thread issued before its stores), then per-group sums.
   {
     constexpr int kPerVec = XF32 ? 4 : 8;  // elements per 16-byte load
-    constexpr int kMaxVec = (R * kGemvMaxKbps * kKB / kPerVec + kGemvRows - 1) / kGemvRows;
+    constexpr int kBatch = 4;               // loads in flight per thread before their stores
     const int per_row = nkb * kKB / kPerVec, nvec = R * per_row;
-    uint4 xv[kMaxVec];
+#pragma unroll 1
+    for (int j0 = 0; j0 * kGemvRows < nvec; j0 += kBatch) {
+    uint4 xv[kBatch];
 #pragma unroll
-    for (int j = 0; j < kMaxVec; ++j) {
+    for (int jj = 0; jj < kBatch; ++jj) {
+      const int j = j0 + jj;
       const int i = t + j * kGemvRows;
-      xv[j] = make_uint4(0, 0, 0, 0);
+      xv[jj] = make_uint4(0, 0, 0, 0);
       if (i < nvec) {
         const int mr = i / per_row, c = i % per_row;
         if (mr < p.m) {
           if (XF32)
-            xv[j] = __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.x) + static_cast<int64_t>(mr) * p.ldx +
-                                                         kb0 * kKB) + c);
+            xv[jj] = __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.x) +
+                                                          static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
           else
-            xv[j] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
-                                                         static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
+            xv[jj] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
+                                                          static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
         }
       }
     }
 #pragma unroll
-    for (int j = 0; j < kMaxVec; ++j) {
-      const int i = t + j * kGemvRows;
+    for (int jj = 0; jj < kBatch; ++jj) {
+      const int i = t + (j0 + jj) * kGemvRows;
       if (i < nvec) {
         const int mr = i / per_row, c = i % per_row;
         float* d = xs + mr * kbps * kKB + c * kPerVec;
-        const uint32_t u[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+        const uint32_t u[4] = {xv[jj].x, xv[jj].y, xv[jj].z, xv[jj].w};
         if (XF32) {
           *reinterpret_cast<float4*>(d) =
               make_float4(__uint_as_float(u[0]), __uint_as_float(u[1]), __uint_as_float(u[2]), __uint_as_float(u[3]));
@@ -834,6 +837,7 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
           }
         }
       }
+    }
     }
   }
   __syncthreads();
@@ -971,20 +975,32 @@ int launch_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
     q.gate = j.gate;
     n_ctas += (j.w->n + qmm::kGemvRows - 1) / qmm::kGemvRows;
   }
-  // Enough CTAs to cover every SM several times, and at most kGemvMaxKbps K blocks per CTA.
-  int split = std::max(1, std::min(qmm::kGemvMaxSplit, (4 * ctx->sm_count + n_ctas - 1) / n_ctas));
-  split = std::max(split, (w0->k_blocks + qmm::kGemvMaxKbps - 1) / qmm::kGemvMaxKbps);
-  if (split > qmm::kGemvMaxSplit)
-    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d needs more than %d K splits", w0->k,
-                     qmm::kGemvMaxSplit);
-  split = std::min(split, w0->k_blocks);
-  const int kbps = (w0->k_blocks + split - 1) / split;
-  // x slice + group sums + partials in dynamic shared memory (<= 200 KB).
+  // The K split (cluster size along K, at most kGemvMaxKbps K blocks per CTA): the one whose CTAs take the
+  // fewest waves of the SMs at the residency their shared memory allows, then the largest (more copies in
+  // flight per output row). Each CTA holds all of its K blocks in shared memory, so a smaller split means
+  // fewer, larger CTAs.
   auto smem_for = [&](int kb) { return qmm::gemv_smem_bytes(R, kb); };
   constexpr size_t kMaxSmem = 200 * 1024;
-  if (smem_for(kbps) > kMaxSmem)
-    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w0->k, R);
-  split = (w0->k_blocks + kbps - 1) / kbps;
+  constexpr size_t kSmPerSm = 228 * 1024;  // shared memory of one SM
+  const int min_split = (w0->k_blocks + qmm::kGemvMaxKbps - 1) / qmm::kGemvMaxKbps;
+  if (min_split > qmm::kGemvMaxSplit)
+    return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d needs more than %d K splits", w0->k,
+                     qmm::kGemvMaxSplit);
+  int split = 0;
+  int64_t best_waves = 0;
+  for (int sp = min_split; sp <= std::min(qmm::kGemvMaxSplit, w0->k_blocks); ++sp) {
+    const int kb = (w0->k_blocks + sp - 1) / sp;
+    if ((w0->k_blocks + kb - 1) / kb != sp || smem_for(kb) > kMaxSmem) continue;  // an empty split, or too big
+    const int64_t per_sm = std::min<int64_t>(16, static_cast<int64_t>(kSmPerSm / (smem_for(kb) + 1024)));
+    const int64_t slots = per_sm * ctx->sm_count;
+    const int64_t waves = (static_cast<int64_t>(n_ctas) * sp + slots - 1) / slots;
+    if (split == 0 || waves <= best_waves) {
+      split = sp;
+      best_waves = waves;
+    }
+  }
+  if (split == 0) return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w0->k, R);
+  const int kbps = (w0->k_blocks + split - 1) / split;
   p.kb_per_split = kbps;
   auto kern = qmm::gemv_kernel<R, XF32>;
   AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem)));

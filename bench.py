@@ -488,7 +488,7 @@ def measure_dit_sp(ctx, dev, world, rank, runs=2):
     eng.close()
     _lib.lib().aex_comm_destroy(comm)
     fl = dit.dit_flops(full)
-    schedule = {0: "ring", 1: "all-gather"}.get(_lib.lib().aex_sp_schedule(world, Jp, full.heads), "?")
+    schedule = {0: "ring", 1: "all-gather", 2: "overlap"}.get(_lib.lib().aex_sp_schedule(world, Jp, full.heads), "?")
     return {"ms_per_4step_denoise": ms, "ms_per_step": ms / 4, "schedule": schedule, "tflops": 4 * fl["total"] / (ms * 1e-3) / 1e12,
             "tflop_per_step": fl["total"] / 1e12, "shard_tokens": Jp, "n_gpus": world, "finite": ok,
             "config": "FLUX.2-klein 2048^2 (J=16,896), 4 steps, one image sequence-parallel "
@@ -578,10 +578,126 @@ def measure_ring(ctx, dev, world, rank, iters=5):
     L.aex_comm_destroy(comm)
     flops = 4.0 * S * S * HEAD_DIM * H
     kv_bytes_per_rank = 2 * Sp * H * HEAD_DIM * 2
-    schedule = {0: "ring", 1: "all-gather"}.get(L.aex_sp_schedule(world, Sp, H), "?")
+    schedule = {0: "ring", 1: "all-gather", 2: "overlap"}.get(L.aex_sp_schedule(world, Sp, H), "?")
     return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "gflop_per_call": flops / 1e9, "seq": S,
             "shard": Sp, "schedule": schedule, "kv_bytes_per_rank": kv_bytes_per_rank,
             "config": "BASELINE configs[4]: 2048^2 joint attention, sequence-parallel over NCCL"}
+
+
+def _rel_err(got, ref):
+    import torch
+
+    d = (got.float() - ref.float())
+    return {"rel_l2": float(d.norm() / ref.float().norm()), "max_abs": float(d.abs().max())}
+
+
+def measure_multi_gpu_parity(ctx, dev, world, rank):
+    """Correctness of the two N-GPU attention paths inside the N-GPU bench itself, against one GPU's
+    aex_joint_attention on the same inputs (every rank builds the same seeded inputs; rank 0 gathers the
+    ranks' outputs over NCCL and compares): the sequence-parallel call (aex_ring_attention, its default
+    schedule) on a 2048^2-shaped joint sequence scaled down to 2 x N x 128 rows, 4 heads, and the head-sharded
+    1024^2 call (24/N heads per GPU). Bar: rel-L2 <= 1e-2 and max-abs <= 2e-2 (the attention tolerance)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from aestrix_b200 import _lib, attention
+
+    L = _lib.lib()
+    res = {}
+    # -- sequence parallel
+    S, H = 2 * world * 128, 4
+    g = torch.Generator().manual_seed(4242)
+    q, k, v = (torch.randn(1, S, H, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    wk = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    ang = torch.rand(S, 64, generator=g) * 6.2831853
+    cos, sin = torch.cos(ang).to(dev), torch.sin(ang).to(dev)
+    Sp = S // world
+    sl = slice(rank * Sp, (rank + 1) * Sp)
+    ql, kl, vl = (t[:, sl].contiguous() for t in (q, k, v))
+    out_l = torch.empty_like(ql)
+    comm = _make_comm(ctx, dev, world, rank)
+    a = attention.make_args(ql, kl, vl, out_l, "bshd", wq, wk, 1e-6, cos[sl].contiguous(), sin[sl].contiguous())
+    stream = torch.cuda.current_stream(dev)
+    ctx.check(L.aex_ring_attention(ctx.handle, comm, C.byref(a), stream.cuda_stream))
+    torch.cuda.synchronize()
+    L.aex_comm_destroy(comm)
+    gathered = [torch.empty_like(out_l) for _ in range(world)]
+    dist.all_gather(gathered, out_l)
+    ref = attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, ctx=ctx, stream=stream)
+    torch.cuda.synchronize()
+    e = _rel_err(torch.cat(gathered, 1), ref)
+    schedule = {0: "ring", 1: "all-gather", 2: "overlap"}.get(L.aex_sp_schedule(world, Sp, H), "?")
+    res["sp_parity"] = dict(e, ok=e["rel_l2"] <= 1e-2 and e["max_abs"] <= 2e-2, seq=S, heads=H, schedule=schedule,
+                            ref="one-GPU aex_joint_attention of the same inputs")
+    # -- head sharded (1024^2, 24/N heads per GPU)
+    hs = HEADS // world
+    g = torch.Generator().manual_seed(4343)
+    q, k, v = (torch.randn(1, SEQ, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    cos_np, sin_np = _rope_tables()
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    h0 = rank * hs
+    out_h = torch.empty(1, SEQ, hs, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    attention.joint_attention(q[:, :, h0:h0 + hs], k[:, :, h0:h0 + hs], v[:, :, h0:h0 + hs], wq, wk, 1e-6, cos, sin,
+                              out=out_h, ctx=ctx, stream=stream)
+    torch.cuda.synchronize()
+    gathered = [torch.empty_like(out_h) for _ in range(world)]
+    dist.all_gather(gathered, out_h)
+    ref = attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, ctx=ctx, stream=stream)
+    torch.cuda.synchronize()
+    e = _rel_err(torch.cat(gathered, 2), ref)
+    res["hs_parity"] = dict(e, ok=e["rel_l2"] <= 1e-2 and e["max_abs"] <= 2e-2, heads_per_gpu=hs,
+                            ref="one-GPU aex_joint_attention of all 24 heads")
+    return res
+
+
+def measure_head_sharded(ctx, dev, world, rank, iters=200):
+    """BASELINE configs[1] split by heads: the 1024^2 joint attention call (4608 tokens, 24 x 128, fused
+    QK-RMSNorm + RoPE) with 24/N heads per GPU and full-sequence Q/K/V on every GPU (strong scaling: the
+    call's total work is fixed). Each rank calls aex_joint_attention on its head slice (strided views, no
+    copy); a call whose CTAs would underfill the SMs splits its keys into ranges merged by log-sum-exp.
+    Device time per call, max over ranks; TFLOP/s = the whole call's 260.9 GFLOP / that time."""
+    import torch
+
+    from aestrix_b200 import _lib, attention
+
+    hs = HEADS // world
+    h0 = rank * hs
+    g = torch.Generator().manual_seed(77 + rank)
+    sets = []
+    for _ in range(2):
+        q, k, v = (torch.randn(1, SEQ, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+        sets.append((q, k, v, torch.empty(1, SEQ, hs, HEAD_DIM, dtype=torch.bfloat16, device=dev)))
+    wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    wk = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+    cos_np, sin_np = _rope_tables()
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def call(i):
+        q, k, v, o = sets[i % 2]
+        attention.joint_attention(q[:, :, h0:h0 + hs], k[:, :, h0:h0 + hs], v[:, :, h0:h0 + hs], wq, wk, 1e-6, cos,
+                                  sin, out=o, ctx=ctx, stream=stream)
+
+    for i in range(5):
+        call(i)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(iters):
+        call(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(world, e0.elapsed_time(e1) / iters)
+    peak, _ = _peaks()
+    tf = FLOPS_PER_CALL / (ms * 1e-3) / 1e12
+    return {"ms": ms, "tflops": tf, "tflops_per_gpu": tf / world, "frac_per_gpu": tf / world / peak,
+            "heads_per_gpu": hs, "key_ranges": _lib.lib().aex_sp_key_ranges(1, SEQ, hs, ctx.sm_count),
+            "scaling": "strong", "n_gpus": world,
+            "config": "BASELINE configs[1]: 1024^2 joint attention, heads split over the GPUs, fused call"}
 
 
 def run_ours(args):
@@ -698,6 +814,8 @@ def run_ours(args):
     e2e_ms = _max_over_ranks(world, ea.elapsed_time(eb) / n_e)
     _barrier(world)
 
+    mg_res = measure_multi_gpu_parity(ctx, dev, world, rank) if world > 1 else None
+    hs_res = measure_head_sharded(ctx, dev, world, rank) if world > 1 and HEADS % world == 0 else None
     i2i_res = measure_i2i(ctx, dev)
     qmm_res = measure_qmm(ctx, dev) if not args.no_qmm else None
     dit_res = measure_dit(ctx, dev, world) if not args.no_dit else None
@@ -727,6 +845,10 @@ def run_ours(args):
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
+        if mg_res is not None:
+            line.update(mg_res)
+        if hs_res is not None:
+            line["head_sharded_1024"] = hs_res
         if dit_res is not None:
             line["dit_denoise"] = dit_res
         if ring_res is not None:
@@ -748,6 +870,47 @@ def run_ours(args):
     return 0
 
 
+def run_kernel_case(args):
+    """A profiling target: one kernel on its standard input and nothing else in the process (no DiT weights,
+    no other workloads), --steps launches after --warmup. attention: the 1024^2 fused call (Q/K/V/O, 113 MB;
+    launches qk_prep_kernel + attn_fwd_kernel); attention_core: the same without norm/RoPE (attn_fwd_kernel
+    alone); gemm: 4-bit linear 4608 x 3072 -> 9216 (gemm_pair_kernel); gemv: 1 x 3072 -> 18432 (gemv_kernel)."""
+    import torch
+
+    from aestrix_b200 import _lib, attention, qmm
+
+    dev = torch.device("cuda", 0)
+    ctx = _lib.context(0)
+    g = torch.Generator().manual_seed(5)
+    if args.kernel_case.startswith("attention"):
+        q, k, v = (torch.randn(1, SEQ, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+        o = torch.empty_like(q)
+        fused = args.kernel_case == "attention"
+        wq = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+        wk = (1 + 0.1 * torch.randn(HEAD_DIM, generator=g)).float().to(dev)
+        cos_np, sin_np = _rope_tables()
+        cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+
+        def call():
+            if fused:
+                attention.joint_attention(q, k, v, wq, wk, 1e-6, cos, sin, out=o, ctx=ctx)
+            else:
+                attention.joint_attention(q, k, v, out=o, ctx=ctx)
+    else:
+        n, m = (9216, 4608) if args.kernel_case == "gemm" else (18432, 1)
+        w = qmm.QuantizedWeight(*qmm.synthetic_weight(n, 3072, seed=n), ctx=ctx)
+        x = torch.randn(m, 3072, generator=g).to(torch.bfloat16).to(dev)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+
+        def call():
+            w(x, out=y)
+    for _ in range(args.warmup + args.steps):
+        call()
+    ctx.sync(None, 60000)
+    emit({"kernel_case": args.kernel_case, "launches": args.warmup + args.steps, "device_status": ctx.device_status()})
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -759,7 +922,11 @@ def main():
     ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 4-step DiT denoise measurement")
     ap.add_argument("--no-ring", action="store_true", help="skip the 2048^2 ring attention and sequence-parallel denoise measurements (N > 1)")
+    ap.add_argument("--kernel-case", choices=["attention", "attention_core", "gemm", "gemv"],
+                    help="run only this kernel on its standard input (a profiling target) and exit")
     args = ap.parse_args()
+    if args.kernel_case:
+        return run_kernel_case(args)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

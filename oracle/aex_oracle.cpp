@@ -137,6 +137,29 @@ void aexo_qmm(const float* x, int m, const uint32_t* packed, const uint16_t* sca
   });
 }
 
+void aexo_qmv(const float* x, int m, const uint32_t* packed, const uint16_t* scales, const uint16_t* biases, int n,
+              int k, int group_size, float* y) {
+  const int groups = k / group_size;
+  parallel_for(n, 16, [&](int64_t r) {
+    const uint32_t* pr = packed + (size_t)r * (k / 8);
+    for (int i = 0; i < m; ++i) {
+      const float* xi = x + (size_t)i * k;
+      double acc = 0.0;
+      for (int g = 0; g < groups; ++g) {
+        double qdot = 0.0, xsum = 0.0;
+        for (int c = g * group_size; c < (g + 1) * group_size; ++c) {
+          const uint32_t q = (pr[c / 8] >> (4 * (c % 8))) & 0xFu;
+          qdot += (double)xi[c] * (double)q;
+          xsum += (double)xi[c];
+        }
+        acc += (double)aexo_bf16_to_f32(scales[(size_t)r * groups + g]) * qdot +
+               (double)aexo_bf16_to_f32(biases[(size_t)r * groups + g]) * xsum;
+      }
+      y[(size_t)i * n + r] = static_cast<float>(acc);
+    }
+  });
+}
+
 void aexo_rope_freqs(const float* ids, int n, float theta, const int* axes_dim, int n_axes, float* cos_out,
                      float* sin_out) {
   int half_total = 0;

@@ -52,6 +52,13 @@ void aexo_pack_q4(const uint8_t* codes, int n, int k, uint32_t* packed);
 void aexo_qmm(const float* x, int m, const uint32_t* packed, const uint16_t* scales, const uint16_t* biases,
               int n, int k, int group_size, float* y);
 
+/* The quantized matrix-vector product of MLX's qmv on f32 activations (the
+ * conditioner's affine_qmm_t_float_gs_64_b_4, DirectConditioner.swift:48,
+ * 183-190): per group, scale * sum(x * q) + bias * sum(x), i.e. the unrounded
+ * dequantized weights, f64 accumulation. */
+void aexo_qmv(const float* x, int m, const uint32_t* packed, const uint16_t* scales, const uint16_t* biases, int n,
+              int k, int group_size, float* y);
+
 /* Flux2RoPE.rope1D / frequencies (Sources/ImarelloCore/Flux2RoPE.swift:16-76):
  * ids [n, n_axes] f32; for each axis of dimension dim_a and i < dim_a/2:
  * omega = 1/pow(theta, 2i/dim_a), angle = pos*omega; cos/sin [n, sum(dim_a/2)]. */

@@ -39,10 +39,13 @@ class DitRef:
         self.bf = bf if storage == "bf16" else _ident
 
     def linear(self, name, x, f32_in=False):
-        """x . deq(W)^T; x rounded to bf16 first (the bf16 qmm) unless f32_in (the f32 qmm)."""
+        """x . deq(W)^T: the bf16 qmm (x rounded to bf16, bf16 dequantized weights), or with f32_in the
+        f32 qmm of the conditioner (MLX qmv: f32 x, unrounded dequantized weights)."""
         p, s, b = self.lin[name]
         n, k = p.shape[0], p.shape[1] * 8
-        return O.qmm(np.asarray(x, np.float32) if f32_in else self.bf(x), p, s, b, n, k)
+        if f32_in:
+            return O.qmv(np.asarray(x, np.float32), p, s, b, n, k)
+        return O.qmm(self.bf(x), p, s, b, n, k)
 
     # DirectConditioner.stepConditioning (:172-213): f32 activations through the f32 qmm.
     def conditioning(self, t):

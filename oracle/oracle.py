@@ -43,6 +43,7 @@ def lib() -> C.CDLL:
         L.aexo_dequant_q4.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int, C.c_int, _u16p]
         L.aexo_pack_q4.argtypes = [_u8p, C.c_int, C.c_int, _u32p]
         L.aexo_qmm.argtypes = [_f32p, C.c_int, _u32p, _u16p, _u16p, C.c_int, C.c_int, C.c_int, _f32p]
+        L.aexo_qmv.argtypes = [_f32p, C.c_int, _u32p, _u16p, _u16p, C.c_int, C.c_int, C.c_int, _f32p]
         L.aexo_rope_freqs.argtypes = [_f32p, C.c_int, C.c_float, _i32p, C.c_int, _f32p, _f32p]
         L.aexo_grid_ids.argtypes = [C.c_int, C.c_int, C.c_float, C.c_float, _f32p]
         L.aexo_text_ids.argtypes = [C.c_int, _f32p]
@@ -108,6 +109,16 @@ def qmm(x, packed, scales, biases, n, k, group_size=64) -> np.ndarray:
     m = x.shape[0]
     y = np.empty((m, n), np.float32)
     lib().aexo_qmm(x, m, _c(packed, np.uint32), _c(scales, np.uint16), _c(biases, np.uint16), n, k, group_size,
+                   y)
+    return y
+
+
+def qmv(x, packed, scales, biases, n, k, group_size=64) -> np.ndarray:
+    """MLX qmv on f32 activations: scale * sum(x * q) + bias * sum(x) per group (unrounded weights)."""
+    x = _c(x, np.float32)
+    m = x.shape[0]
+    y = np.empty((m, n), np.float32)
+    lib().aexo_qmv(x, m, _c(packed, np.uint32), _c(scales, np.uint16), _c(biases, np.uint16), n, k, group_size,
                    y)
     return y
 

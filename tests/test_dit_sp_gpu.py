@@ -2,8 +2,9 @@
 one-GPU engine on the whole sequence: the small config (hidden 256 = 2 heads,
 1 double + 2 single blocks, 32 text + 8x8 image tokens) split into two equal
 contiguous shards (rank 0: the 32 text rows + 16 image rows; rank 1: 48 image
-rows), joint attention over NCCL under both exchange schedules (ring; one
-all-gather), 3-step denoise. Tolerance: relative L2 <= 2e-2 on each rank's
+rows), joint attention over NCCL under the three exchange schedules (ring; one
+all-gather; pairwise exchanges overlapped with per-shard attention), 3-step
+denoise. Tolerance: relative L2 <= 2e-2 on each rank's
 latents (bf16 activations; the ring merges per-hop bf16 partial outputs by
 log-sum-exp). Skips with fewer than 2 GPUs."""
 import ctypes as C
@@ -93,7 +94,7 @@ def _worker(rank, world, port, out_dir, schedule):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("schedule", ["ring", "gather"])
+@pytest.mark.parametrize("schedule", ["ring", "gather", "overlap"])
 def test_dit_sequence_parallel_two_gpus(tmp_path, schedule):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

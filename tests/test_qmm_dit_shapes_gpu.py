@@ -12,14 +12,15 @@
 
 Each output is checked twice: every row against an fp32 matmul of the bit-exact
 dequantized weights (aex_dequantize_mlx, itself bit-exact with the oracle), and a
-sample of rows against the oracle's restatement of quantizedMM (O.qmm, f64
-accumulation). Tolerances as tests/test_qmm_gpu.py: the tensor-core path (M > 16)
-in f32 output within 1e-4 relative (same bf16 weights, only the summation order
-differs), the GEMV path (M <= 16, MLX qmv's unrounded-weight formulation) within
-5e-3; bf16 output within rel-L2 1e-2 / max-abs 2e-2 of the output's magnitude.
-The M = 1 rows with K <= 4096 (the conditioner's K = 256 and 3072) also run with f32
-activations, the reference's f32 qmm (DirectConditioner.swift:48, 183-190); f32
-activations take the GEMV path only, so larger K returns AEX_ERR_UNSUPPORTED."""
+sample of rows against the oracle: the tensor-core path (M > 16) against O.qmm
+(quantizedMM on bf16 dequantized weights, f64 accumulation) within 1e-4 relative
+(same weights, only the summation order differs); the GEMV path (M <= 16) against
+O.qmv (MLX qmv: scale * sum(x q) + bias * sum(x), the unrounded weights, f64)
+within 1e-4, and against the bf16-weight matmul within 5e-3 (the weight rounding);
+bf16 output within rel-L2 1e-2 / max-abs 2e-2 of the output's magnitude.
+The M = 1 rows with K <= 8192 (the conditioner's K = 256 and 3072 among them) also run
+with f32 activations, the reference's f32 qmm (DirectConditioner.swift:48, 183-190); f32
+activations take the GEMV path only (K <= 8192), so larger K returns AEX_ERR_UNSUPPORTED."""
 import numpy as np
 import pytest
 import torch
@@ -77,10 +78,11 @@ def test_qmm_every_dit_shape(cuda_ctx, k, n, m):
     rl2, mx = _rel(y16.float().cpu().numpy(), full.cpu().numpy())
     assert rl2 <= 1e-2 and mx <= 2e-2, f"bf16 out vs fp32 matmul: rel-L2 {rl2:.3e} max {mx:.3e}"
     rows = np.unique(np.linspace(0, m - 1, min(m, 12)).astype(int))
-    ref = O.qmm(x[rows].float().cpu().numpy(), p, s, b, n, k)
+    gemv = m <= 16 and k <= 8192  # the GEMV path: at most 8 K splits x 16 K blocks
+    ref = (O.qmv if gemv else O.qmm)(x[rows].float().cpu().numpy(), p, s, b, n, k)
     rl2, mx = _rel(y32.cpu().numpy()[rows], ref)
-    assert rl2 <= tol and mx <= 2 * tol, f"f32 out vs oracle rows: rel-L2 {rl2:.3e} max {mx:.3e}"
-    if m == 1 and k > 4096:
+    assert rl2 <= 1e-4 and mx <= 2e-4, f"f32 out vs oracle rows: rel-L2 {rl2:.3e} max {mx:.3e}"
+    if m == 1 and k > 8192:
         with pytest.raises(_lib.AexError) as e:
             w(torch.randn(1, k, generator=g).cuda(), out_dtype=torch.float32)
         assert e.value.code == _lib.AEX_ERR_UNSUPPORTED
@@ -88,7 +90,7 @@ def test_qmm_every_dit_shape(cuda_ctx, k, n, m):
         xf = torch.randn(1, k, generator=g).cuda()  # f32 activations, not bf16-representable
         yf = w(xf, out_dtype=torch.float32)
         torch.cuda.synchronize()
-        ref = O.qmm(xf.cpu().numpy(), p, s, b, n, k)
+        ref = O.qmv(xf.cpu().numpy(), p, s, b, n, k)
         rl2, mx = _rel(yf.cpu().numpy(), ref)
-        assert rl2 <= 5e-3 and mx <= 1e-2, f"f32 x vs oracle: rel-L2 {rl2:.3e} max {mx:.3e}"
+        assert rl2 <= 1e-4 and mx <= 2e-4, f"f32 x vs oracle qmv: rel-L2 {rl2:.3e} max {mx:.3e}"
     assert cuda_ctx.device_status() == 0

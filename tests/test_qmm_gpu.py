@@ -7,7 +7,8 @@
   an fp32 matmul of the bit-exact dequantized weights. Tolerances: relative L2 <= 1e-2
   (bf16 output) and max-abs <= 2e-2 relative to the output's max magnitude; f32 output
   of the tensor-core path (m > 16) within 1e-4, of the GEMV path (m <= 16, which like
-  MLX's qmv uses the unrounded dequantized weights) within 5e-3.
+  MLX's qmv uses the unrounded dequantized weights) within 1e-4 of the oracle's qmv
+  and 5e-3 of the bf16-weight product.
 """
 import json
 import os
@@ -87,7 +88,10 @@ def test_qmm_vs_oracle(cuda_ctx, m, n, k):
         # tensor-core path: the bit-exact bf16 weights, f32 accumulation (order differs only)
         _assert_close(y32.cpu().numpy(), ref, rel=1e-4, absr=1e-4)
     else:
-        # GEMV path: scale*sum(x*q) + bias*sum(x) with unrounded weights (MLX qmv's formulation)
+        # GEMV path: scale*sum(x*q) + bias*sum(x) with unrounded weights (MLX qmv's formulation): against the
+        # oracle's qmv (f64) tightly, against the bf16-weight product within the weight rounding
+        qv = O.qmv(x.float().numpy(), _np_u32(packed), _np_u16(scales), _np_u16(biases), n, k)
+        _assert_close(y32.cpu().numpy(), qv, rel=1e-4, absr=2e-4)
         _assert_close(y32.cpu().numpy(), ref, rel=5e-3, absr=1e-2)
     _assert_close(y16.float().cpu().numpy(), ref)
 

@@ -1,11 +1,17 @@
-"""CPU (gloo, world size 2 and 3) tests of the two exchange schedules of
+"""CPU (gloo, world size 2 to 4) tests of the exchange schedules of
 aex_ring_attention against the full-sequence oracle, on contiguous sequence
-shards: the ring (K/V passed to rank r+1 each hop, partial results merged by
-their log2-sum-exp; the hop/peer schedule and merge formula of
-aestrix_b200/csrc/ring_attention.cpp and ring_kernels.cu) and the all-gather
-(every rank's K/V written token-major into slot r of one buffer, gathered in
-place, then one attention over all keys). Also the schedule choice of
-aex_sp_schedule (host logic, no GPU)."""
+shards:
+* overlap (the default for more than one rank): the plan comes from the
+  library itself (aex_sp_plan, the host logic ring_attention.cpp runs on the
+  GPU path), and each rank executes its steps in order with gloo point-to-point
+  transfers and numpy attention partials, merged with the formula of
+  merge_splits_kernel;
+* the ring (K/V passed to rank r+1 each hop, partial results merged by their
+  log2-sum-exp; the hop/peer schedule and merge formula of
+  aestrix_b200/csrc/ring_attention.cpp and ring_kernels.cu);
+* the all-gather (every rank's K/V written token-major into slot r of one
+  buffer, gathered in place, then one attention over all keys).
+Also the schedule choice of aex_sp_schedule (host logic, no GPU)."""
 import subprocess
 import sys
 import datetime
@@ -107,16 +113,97 @@ def test_gather_schedule_gloo(world):
     assert max(result.values()) < 1e-5, dict(result)
 
 
+def _overlap_worker(rank, world, port, S, H, result):
+    from aestrix_b200 import _lib
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    rng = np.random.default_rng(5)
+    q, k, v = (rng.standard_normal((S, H, 128)).astype(np.float32) for _ in range(3))
+    Sp = S // world
+    sl = slice(rank * Sp, (rank + 1) * Sp)
+    slots = {rank: np.stack([k[sl], v[sl]])}  # K/V slot r: rank r's shard, as in K_all / V_all
+    landed = {}  # exchange index -> slot it filled
+    parts = {}
+    out = None
+    for op in _lib.sp_plan(world, rank):
+        if op.kind == _lib.AEX_SP_OP_EXCHANGE:
+            recv = torch.empty((2, Sp, H, 128), dtype=torch.float32)
+            reqs = [dist.isend(torch.from_numpy(slots[rank]), op.send_to), dist.irecv(recv, op.recv_from)]
+            for r in reqs:
+                r.wait()
+            assert op.recv_from not in slots
+            slots[op.recv_from] = recv.numpy()
+            landed[op.part] = op.recv_from
+        elif op.kind == _lib.AEX_SP_OP_ATTEND:
+            if op.wait_exchange >= 0:  # reads exactly the shard that exchange delivered
+                assert landed[op.wait_exchange] == op.slot
+            else:
+                assert op.slot == rank
+            kv = slots[op.slot]
+            assert np.array_equal(kv[0], k[op.slot * Sp:(op.slot + 1) * Sp])
+            assert op.part not in parts
+            parts[op.part] = _partial(q[sl], kv[0], kv[1], 1 / np.sqrt(128))
+        else:  # merge_splits_kernel: sum_r 2^(lse_r - max) o_r / sum_r 2^(lse_r - max)
+            assert sorted(parts) == list(range(op.part)) and op.part == world
+            lse = np.stack([parts[r][1] for r in range(op.part)])  # [P, H, S]
+            w = np.exp2(lse - lse.max(0, keepdims=True))
+            out = sum(w[r].T[..., None] * parts[r][0] for r in range(op.part)) / w.sum(0).T[..., None]
+    assert sorted(slots) == list(range(world))
+    ref = O.sdpa(q[None], k[None], v[None], 1 / np.sqrt(128))[0]
+    result[rank] = float(np.abs(out - ref[sl]).max())
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_overlap_plan_gloo(world):
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    mp.start_processes(_overlap_worker, args=(world, _free_port(), 64 * world, 2, result), nprocs=world, join=True,
+                       start_method="spawn")
+    assert len(result) == world
+    assert max(result.values()) < 1e-5, dict(result)
+
+
+def test_overlap_plan_shape():
+    """Every rank's plan: the local shard's attention first, P - 1 exchanges whose pairs match across ranks
+    (rank r sends to r + h exactly when rank r + h receives from r in the same exchange h), one attention per
+    shard on alternating streams, one merge of all P partials; bad arguments give -1."""
+    from aestrix_b200 import _lib
+
+    for world in (1, 2, 5, 8, 16):
+        plans = [_lib.sp_plan(world, r) for r in range(world)]
+        for r, plan in enumerate(plans):
+            kinds = [op.kind for op in plan]
+            assert kinds == [1] + [0] * (world - 1) + [1] * (world - 1) + [2]
+            assert plan[0].slot == r and plan[0].wait_exchange == -1 and plan[0].part == 0
+            for op in plan[1:world]:
+                h = op.part
+                peer = plans[op.send_to][h]
+                assert peer.kind == 0 and peer.recv_from == r
+            attends = plan[world:2 * world - 1]
+            assert sorted(op.slot for op in plan if op.kind == 1) == list(range(world))
+            assert [op.stream for op in attends] == [h & 1 for h in range(1, world)]
+            assert plan[-1].part == world
+    L = _lib.lib()
+    assert L.aex_sp_plan(17, 0, None, 0) == -1
+    assert L.aex_sp_plan(4, 4, None, 0) == -1
+    assert L.aex_sp_plan(4, 1, (_lib.aex_sp_op * 2)(), 2) == -1  # too few entries
+
+
 _SCHEDULE_PROBE = (
     "import sys; sys.path.insert(0, sys.argv[1]); from aestrix_b200 import _lib; L = _lib.lib(); "
     "print(L.aex_sp_schedule(8, 2112, 24), L.aex_sp_schedule(2, 8448, 24), L.aex_sp_schedule(8, 1 << 20, 24), "
-    "L.aex_sp_schedule(0, 2112, 24), L.aex_sp_schedule(2, 0, 24))")
+    "L.aex_sp_schedule(1, 2112, 24), L.aex_sp_schedule(0, 2112, 24), L.aex_sp_schedule(2, 0, 24))")
 
 
-@pytest.mark.parametrize("env,want", [(None, "1 1 0 -1 -1"), ("ring", "0 0 0 -1 -1"), ("gather", "1 1 1 -1 -1")])
+@pytest.mark.parametrize("env,want", [(None, "2 2 0 1 -1 -1"), ("ring", "0 0 0 0 -1 -1"), ("gather", "1 1 1 1 -1 -1"),
+                                      ("overlap", "2 2 2 2 -1 -1")])
 def test_sp_schedule_choice(env, want):
-    """All-gather while the gathered K/V (2 * world * seq * heads * 256 bytes) fit in 8 GiB, ring beyond;
-    AEX_SP_SCHEDULE overrides. Each case in a fresh process: the override is read once."""
+    """Overlap for more than one rank while the gathered K/V (2 * world * seq * heads * 256 bytes) fit in 8 GiB,
+    all-gather for one rank, ring beyond; AEX_SP_SCHEDULE overrides. Each case in a fresh process: the override
+    is read once."""
     e = {k: v for k, v in os.environ.items() if k != "AEX_SP_SCHEDULE"}
     if env:
         e["AEX_SP_SCHEDULE"] = env

@@ -1,8 +1,8 @@
 """aex_ring_attention on 2 GPUs (one process per GPU, NCCL over NVLink) against
 the full-sequence oracle: fused QK-RMSNorm + RoPE + SDPA of the joint sequence
-split into contiguous shards, under both exchange schedules (ring of
-point-to-point hops; one all-gather); the 2-rank cases skip on a box with
-fewer than 2 GPUs. On one GPU, a 1-rank communicator runs the all-gather
+split into contiguous shards, under the three exchange schedules (ring of
+point-to-point hops; one all-gather; pairwise exchanges overlapped with
+per-shard attention); the 2-rank cases skip on a box with fewer than 2 GPUs. On one GPU, a 1-rank communicator runs the all-gather
 schedule's attention split into key ranges.
 Tolerance: relative L2 <= 1e-2, max-abs <= 2e-2 (as the single-GPU attention)."""
 import ctypes as C
@@ -74,7 +74,7 @@ def _worker(rank, world, port, l_txt, grid, heads, out_dir, schedule):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("schedule", ["ring", "gather"])
+@pytest.mark.parametrize("schedule", ["ring", "gather", "overlap"])
 @pytest.mark.parametrize("l_txt,grid,heads", [(64, 24, 4), (512, 128, 2)])
 def test_ring_attention_two_gpus(tmp_path, l_txt, grid, heads, schedule):
     if torch.cuda.device_count() < 2:
