@@ -69,13 +69,17 @@ CONFIG = {
 }
 
 
-def _peaks():
+def _peaks(sustained: bool = False):
+    """The bf16 denominator: the measured burst figure (a kernel timed alone at full clock) or, with
+    sustained, the measured power-capped figure (a kernel timed while the 1000 W cap holds the clock down)."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
+        if sustained:
+            return float(p["bf16_tflops_sustained"]), "measured"
         return float(p["bf16_tflops"]), "measured"
     except Exception:
-        return 1590.0, "fallback"
+        return (1400.0 if sustained else 1590.0), "fallback"
 
 
 def _hbm_peak():
@@ -742,7 +746,6 @@ def run_ours(args):
     torch.cuda.synchronize()
     clk_end = clk.mark()
     _barrier(world)
-    clk.__exit__()
     clocks = clk.summary(clk_mark, clk_end) if clk_end > clk_mark else dict(
         clk.summary(clk.n_pre), note="no sample fell inside the timed region: samples from warm-up through timing")
     ms_local = ev0.elapsed_time(ev1) / args.steps
@@ -756,6 +759,7 @@ def run_ours(args):
         attention.joint_attention(q, k, v, out=o, ctx=ctx, stream=stream)
     ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_k = min(max(args.steps, 10), 400)
+    k_mark = clk.mark()
     ka.record(stream)
     for i in range(n_k):
         q, k, v, o = sets[i % N_INPUT_SETS]
@@ -763,6 +767,8 @@ def run_ours(args):
     kb.record(stream)
     torch.cuda.synchronize()
     kernel_ms = ka.elapsed_time(kb) / n_k
+    k_clocks = clk.summary(k_mark, clk.mark())
+    clk.__exit__()
     ctx.sync(stream.cuda_stream)
 
     # ---- end to end through the C ABI with host buffers (H2D inputs, D2H output per step)
@@ -822,19 +828,24 @@ def run_ours(args):
     ring_res = measure_ring(ctx, dev, world, rank) if (world > 1 and not args.no_ring) else None
     sp_res = measure_dit_sp(ctx, dev, world, rank) if (world > 1 and not args.no_ring and not args.no_dit) else None
     if rank == 0:
-        peak, peak_kind = _peaks()
+        # The kernel-alone loop right after a long timed region can run under the 1000 W cap: then the
+        # power-capped (sustained) cuBLAS figure is the fair denominator, else the burst one.
+        capped = "sw_power_cap" in (k_clocks.get("reasons") or [])
+        peak, peak_kind = _peaks(sustained=capped)
+        peak_kind = (f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops_sustained: the kernel loop ran under sw_power_cap)"
+                     if capped else f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)")
         achieved = FLOPS_PER_CALL / (kernel_ms * 1e-3) / 1e12
         tf_cpu, dt_cpu, sample, cores = cpu_baseline_sample(rows=args.cpu_rows)
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
-            "pct_bf16_peak": 100.0 * value / world / peak,
+            "pct_bf16_peak": 100.0 * value / world / _peaks(sustained="sw_power_cap" in (clocks.get("reasons") or []))[0],
             "roofline": {"bound": "tensor", "kernel": "attn_fwd_kernel", "achieved": achieved, "peak": peak,
-                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)", "unit": "TFLOP/s",
+                         "peak_kind": peak_kind, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": _traffic_from_profile(),
                          "algorithmic": f"{FLOPS_PER_CALL / 1e9:.1f} GFLOP per launch (4*S^2*D*H)",
-                         "kernel_ms": kernel_ms},
+                         "kernel_ms": kernel_ms, "kernel_clocks": k_clocks},
             "cpu_baseline": {"value": tf_cpu, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample,
                              "seconds": dt_cpu},
             "e2e": {"value": world * FLOPS_PER_CALL / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
@@ -874,7 +885,8 @@ def run_kernel_case(args):
     """A profiling target: one kernel on its standard input and nothing else in the process (no DiT weights,
     no other workloads), --steps launches after --warmup. attention: the 1024^2 fused call (Q/K/V/O, 113 MB;
     launches qk_prep_kernel + attn_fwd_kernel); attention_core: the same without norm/RoPE (attn_fwd_kernel
-    alone); gemm: 4-bit linear 4608 x 3072 -> 9216 (gemm_pair_kernel); gemv: 1 x 3072 -> 18432 (gemv_kernel)."""
+    alone); gemm: 4-bit linear 4608 x 3072 -> 9216 (gemm_pair_kernel); gemv: 1 x 3072 -> 18432 (gemv_kernel);
+    dit: the 1024^2 FLUX.2-klein engine (weights uploaded and unpacked first), then --steps 4-step denoises."""
     import torch
 
     from aestrix_b200 import _lib, attention, qmm
@@ -882,7 +894,24 @@ def run_kernel_case(args):
     dev = torch.device("cuda", 0)
     ctx = _lib.context(0)
     g = torch.Generator().manual_seed(5)
-    if args.kernel_case.startswith("attention"):
+    if args.kernel_case == "dit":
+        from aestrix_b200 import dit
+
+        cfg = dit.DitConfig()
+        lin, norms = dit.random_weights(cfg, seed=11, device=dev)
+        eng = dit.DitEngine(cfg, ctx=ctx)
+        eng.load(lin, norms)
+        del lin
+        cos, sin = dit.rope_tables(cfg, device=dev)
+        eng.set_rope(cos, sin)
+        eng.project_context(torch.randn(cfg.l_txt, cfg.text_dim, generator=g).to(torch.bfloat16).to(dev))
+        lat = torch.randn(cfg.l_img, cfg.in_channels, generator=g).to(dev)
+
+        def call():
+            eng.denoise(lat.clone(), steps=4)
+
+        args.warmup = 0
+    elif args.kernel_case.startswith("attention"):
         q, k, v = (torch.randn(1, SEQ, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
         o = torch.empty_like(q)
         fused = args.kernel_case == "attention"
@@ -922,7 +951,7 @@ def main():
     ap.add_argument("--no-qmm", action="store_true", help="skip the secondary 4-bit linear measurements")
     ap.add_argument("--no-dit", action="store_true", help="skip the secondary 4-step DiT denoise measurement")
     ap.add_argument("--no-ring", action="store_true", help="skip the 2048^2 ring attention and sequence-parallel denoise measurements (N > 1)")
-    ap.add_argument("--kernel-case", choices=["attention", "attention_core", "gemm", "gemv"],
+    ap.add_argument("--kernel-case", choices=["attention", "attention_core", "gemm", "gemv", "dit"],
                     help="run only this kernel on its standard input (a profiling target) and exit")
     args = ap.parse_args()
     if args.kernel_case:
