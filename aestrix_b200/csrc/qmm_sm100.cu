@@ -712,10 +712,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 // ------------------------------------------------------------------ GEMV
 // A CTA owns 128 weight rows (outputs) — exactly one half of a 256-row tile, so
 // its weights for a K block are one contiguous 4608-byte half-chunk — and one
-// K split of the cluster. Thread 0 bulk-copies every half-chunk of the split
-// into shared memory at once (one mbarrier per K block; the copy engine keeps
-// HBM busy without per-thread loads in flight), the threads stage x meanwhile
-// and then take the K blocks in order as they land, one weight row each.
+// K split of the cluster. The split's half-chunks stream through a ring of
+// kGemvRing shared-memory slots: thread 0 bulk-copies the first kGemvRing at
+// once (one mbarrier per slot; the copy engine keeps HBM busy without
+// per-thread loads in flight) and refills a slot as soon as every thread has
+// used it; the threads stage x meanwhile and then take the K blocks in order as
+// they land, one weight row each. The ring keeps the shared memory of a CTA
+// small, so even a 3072 x 18432 weight (215 KB per SM) runs in one wave.
 // Partial sums of the cluster's splits are reduced in CTA rank 0 through
 // distributed shared memory (no scratch, no atomics, fixed order).
 // One launch may cover up to kGemvMaxProblems weights that read the same x
@@ -726,7 +729,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 // staged as f32 either way, so the arithmetic is the same.
 constexpr int kGemvRows = 128;
 constexpr int kGemvMaxSplit = 8;   // cluster size along K (portable limit)
-constexpr int kGemvMaxKbps = 16;   // K blocks per CTA
+constexpr int kGemvMaxKbps = 48;   // K blocks per CTA
+constexpr int kGemvRing = 4;       // weight slots per CTA
 constexpr int kGemvMaxProblems = 4;
 
 struct GemvProblem {
@@ -750,9 +754,9 @@ struct GemvParams {
 
 // Shared memory of gemv_kernel<R> for `kbps` K blocks per CTA.
 __host__ __device__ constexpr size_t gemv_smem_bytes(int R, int kbps) {
-  return static_cast<size_t>(kbps) * kHalfBytes                                   // weight half-chunks
+  return static_cast<size_t>(kGemvRing) * kHalfBytes                              // weight ring
          + static_cast<size_t>(R) * (kbps * kKB + kbps + kGemvRows) * 4          // x, group sums, partials
-         + 8 + static_cast<size_t>(kbps) * 8;                                    // align + barriers
+         + 8 + static_cast<size_t>(kGemvRing) * 8;                               // align + barriers
 }
 
 template <int R, bool XF32>
@@ -760,7 +764,7 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
   extern __shared__ __align__(16) uint8_t gsm_raw[];
   const int kbps = p.kb_per_split;
   uint8_t* wsm = gsm_raw;
-  float* xs = reinterpret_cast<float*>(gsm_raw + static_cast<size_t>(kbps) * kHalfBytes);
+  float* xs = reinterpret_cast<float*>(gsm_raw + static_cast<size_t>(kGemvRing) * kHalfBytes);
   float* gsum = xs + R * kbps * kKB;
   float* part = gsum + R * kbps;
   uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(part + R * kGemvRows) + 7) & ~uintptr_t(7));
@@ -779,20 +783,22 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
   const int row = cta * kGemvRows + t;  // weight row (output column)
   const int nt = cta >> 1, half = cta & 1;
   const bool active = row < q.n;
-  // 1. Barriers, then every weight copy of this CTA's K range.
+  // 1. Barriers, then the first kGemvRing weight copies of this CTA's K range.
+  auto issue = [&](int g) {  // K block g of the range into slot g % kGemvRing (thread 0)
+    uint64_t* bar = &bars[g % kGemvRing];
+    mbar_arrive_expect_tx(bar, kHalfBytes);
+    bulk_load(wsm + (g % kGemvRing) * kHalfBytes,
+              q.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes, kHalfBytes, bar);
+  };
   if (t == 0) {
     abort_flag = 0;
-    for (int g = 0; g < nkb; ++g) mbar_init(&bars[g], 1);
+    for (int s = 0; s < kGemvRing; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
   }
   __syncthreads();
-  if (t == 0) {
-    for (int g = 0; g < nkb; ++g) {
-      mbar_arrive_expect_tx(&bars[g], kHalfBytes);
-      bulk_load(wsm + g * kHalfBytes, q.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes, kHalfBytes,
-                &bars[g]);
-    }
-  }
+  int issued = 0;  // copies issued (thread 0)
+  if (t == 0)
+    for (; issued < nkb && issued < kGemvRing; ++issued) issue(issued);
   // 2. Stage this split's x slice as f32 (16-byte loads: x 16-byte aligned and its row pitch a multiple of 16
   //    bytes, checked on the host; every load of a thread issued before its stores), then per-group sums.
   {
@@ -861,10 +867,13 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
   for (int mr = 0; mr < R; ++mr) acc[mr] = 0.f;
   int landed = 0;
   for (int g = 0; g < nkb; ++g) {
-    if (!mbar_wait(&bars[g], 0, &abort_flag, p.status, kDevTimeoutTma)) break;
+    const bool got = mbar_wait(&bars[g % kGemvRing], (g / kGemvRing) & 1, &abort_flag, p.status, kDevTimeoutTma);
+    // Uniform across the CTA: block g has landed and every thread is done with block g - 1.
+    if (!__syncthreads_and(got)) break;
     landed = g + 1;
+    if (t == 0 && g >= 1 && issued < nkb) issue(issued++);  // refill the slot block g - 1 used
     if (!active) continue;
-    const uint8_t* hb = wsm + g * kHalfBytes;
+    const uint8_t* hb = wsm + (g % kGemvRing) * kHalfBytes;
     const uint4 w0 = *reinterpret_cast<const uint4*>(hb + t * 32);
     const uint4 w1 = *reinterpret_cast<const uint4*>(hb + t * 32 + 16);
     const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4096 + t * 2));
@@ -898,10 +907,10 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
   }
   if (landed < nkb && t == 0) {
     // Aborting: let the copies still in flight land before the CTA can exit.
-    for (int g = landed; g < nkb; ++g) {
-      const uint32_t a = smem_u32(&bars[g]);
+    for (int g = landed; g < issued; ++g) {
+      const uint32_t a = smem_u32(&bars[g % kGemvRing]);
       const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(a, 0) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
+      while (!mbar_try_wait(a, (g / kGemvRing) & 1) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
       }
     }
   }
@@ -977,8 +986,7 @@ int launch_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
   }
   // The K split (cluster size along K, at most kGemvMaxKbps K blocks per CTA): the one whose CTAs take the
   // fewest waves of the SMs at the residency their shared memory allows, then the largest (more copies in
-  // flight per output row). Each CTA holds all of its K blocks in shared memory, so a smaller split means
-  // fewer, larger CTAs.
+  // flight per output row).
   auto smem_for = [&](int kb) { return qmm::gemv_smem_bytes(R, kb); };
   constexpr size_t kMaxSmem = 200 * 1024;
   constexpr size_t kSmPerSm = 228 * 1024;  // shared memory of one SM

@@ -197,7 +197,7 @@ int aex_qmm(aex_ctx* ctx, const aex_qweight* w, const void* x, int64_t ldx, int 
 
 /* aex_qmm with the activation dtype chosen: x_dtype AEX_DTYPE_BF16 (as
  * aex_qmm) or AEX_DTYPE_F32 (row pitch ldx a multiple of 4 elements; m <= 16
- * and k <= 8192, else AEX_ERR_UNSUPPORTED). Reference: the conditioner's f32 qmm
+ * and k <= 24576, else AEX_ERR_UNSUPPORTED). Reference: the conditioner's f32 qmm
  * affine_qmm_t_float_gs_64_b_4 on f32 activations (timestep MLP, modulation
  * heads, norm_out; Sources/ImarelloDirect/DirectConditioner.swift:48,98-116,
  * 183-190). The dot keeps f32 throughout: y = sum_g scale_g * sum(x * q) +

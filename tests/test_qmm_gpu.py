@@ -84,7 +84,7 @@ def test_qmm_vs_oracle(cuda_ctx, m, n, k):
     y32 = w(x.cuda(), out_dtype=torch.float32)
     y16 = w(x.cuda())
     torch.cuda.synchronize()
-    if m > 16 or k > 8192:
+    if m > 16 or k > 24576:
         # tensor-core path: the bit-exact bf16 weights, f32 accumulation (order differs only)
         _assert_close(y32.cpu().numpy(), ref, rel=1e-4, absr=1e-4)
     else:
@@ -130,6 +130,20 @@ def test_qmm_strided_io_and_errors(cuda_ctx):
     assert e.value.code == _lib.AEX_ERR_UNSUPPORTED
     with pytest.raises(_lib.AexError):
         w(torch.zeros(4, k + 8, dtype=torch.bfloat16, device="cuda")[:, 4:4 + k])  # 8-byte misaligned rows
+    assert cuda_ctx.device_status() == 0
+
+
+def test_f32_activations_outside_the_gemv_path_are_rejected(cuda_ctx):
+    """f32 activations run on the GEMV path only: m > 16 or K > 24576 returns AEX_ERR_UNSUPPORTED, launching
+    nothing."""
+    w = qmm.QuantizedWeight(*qmm.synthetic_weight(128, 256, seed=4))
+    with pytest.raises(_lib.AexError) as e:
+        w(torch.zeros(17, 256, device="cuda"), out_dtype=torch.float32)
+    assert e.value.code == _lib.AEX_ERR_UNSUPPORTED
+    wk = qmm.QuantizedWeight(*qmm.synthetic_weight(128, 24576 + 64, seed=5))
+    with pytest.raises(_lib.AexError) as e:
+        wk(torch.zeros(1, 24576 + 64, device="cuda"), out_dtype=torch.float32)
+    assert e.value.code == _lib.AEX_ERR_UNSUPPORTED
     assert cuda_ctx.device_status() == 0
 
 
