@@ -69,6 +69,13 @@ __device__ __forceinline__ uint32_t code_pair_128(uint32_t wp, int j) {
   return ((wp >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
 }
 
+// Byte `b` (0..3) of a word whose bytes each hold a code in their low nibble,
+// as the exact f32 128 + q: 0x43 is the top byte of f32 128.0 and the code
+// lands in mantissa bits 16..19 (one byte permute).
+__device__ __forceinline__ float code_f32_128(uint32_t v, int b) {
+  return __uint_as_float(__byte_perm(v, 0x43u, 0x4055u | (static_cast<uint32_t>(b) << 8)));
+}
+
 // Exact dequant of a permuted word (the reference's f32 scale*q + bias, then
 // RNE to bf16), 8 bf16 in K order.
 __device__ __forceinline__ uint4 dequant_word_exact(uint32_t wp, float s, float b) {
@@ -879,30 +886,40 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
     const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4096 + t * 2));
     const float bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4352 + t * 2));
     const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    float2 tq[R];
+    // Two accumulator pairs per row (codes 0,1,4,5 and 2,3,6,7 of each word) at R = 1 for a shorter
+    // dependency chain; one pair per row otherwise.
+    constexpr int kAcc = R == 1 ? 2 : 1;
+    float2 tq[R][kAcc];
 #pragma unroll
-    for (int mr = 0; mr < R; ++mr) tq[mr] = make_float2(0.f, 0.f);
+    for (int mr = 0; mr < R; ++mr)
+#pragma unroll
+      for (int a = 0; a < kAcc; ++a) tq[mr][a] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
+      // Codes 2j / 2j+1 of a permuted word sit at bits 4j / 16+4j, so the low nibbles of its bytes are codes
+      // 0, 4, 1, 5 and the high nibbles codes 2, 6, 3, 7; one byte permute per code makes the f32 128 + q.
+      const uint32_t lo = ws[c] & 0x0F0F0F0Fu, hi = (ws[c] >> 4) & 0x0F0F0F0Fu;
+      const float2 q01 = make_float2(code_f32_128(lo, 0), code_f32_128(lo, 2));
+      const float2 q23 = make_float2(code_f32_128(hi, 0), code_f32_128(hi, 2));
+      const float2 q45 = make_float2(code_f32_128(lo, 1), code_f32_128(lo, 3));
+      const float2 q67 = make_float2(code_f32_128(hi, 1), code_f32_128(hi, 3));
+      const int kk = g * kKB + c * 8;  // codes kk .. kk+7
 #pragma unroll
-      for (int i = 0; i < 4; i += 2) {
-        // codes 2i .. 2i+3 of the (permuted) word as f32 128 + q
-        const uint32_t t0 = code_pair_128(ws[c], i), t1 = code_pair_128(ws[c], i + 1);
-        const float2 q0 = make_float2(__uint_as_float(t0 << 16), __uint_as_float(t0 & 0xFFFF0000u));
-        const float2 q1 = make_float2(__uint_as_float(t1 << 16), __uint_as_float(t1 & 0xFFFF0000u));
-        const int kk = g * kKB + c * 8 + 2 * i;  // codes kk .. kk+3
-#pragma unroll
-        for (int mr = 0; mr < R; ++mr) {
-          const float4 x4 = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
-          tq[mr] = ffma2(q0, make_float2(x4.x, x4.y), tq[mr]);
-          tq[mr] = ffma2(q1, make_float2(x4.z, x4.w), tq[mr]);
-        }
+      for (int mr = 0; mr < R; ++mr) {
+        const float4 xa = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
+        const float4 xb = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk + 4);
+        tq[mr][0] = ffma2(q01, make_float2(xa.x, xa.y), tq[mr][0]);
+        tq[mr][kAcc - 1] = ffma2(q23, make_float2(xa.z, xa.w), tq[mr][kAcc - 1]);
+        tq[mr][0] = ffma2(q45, make_float2(xb.x, xb.y), tq[mr][0]);
+        tq[mr][kAcc - 1] = ffma2(q67, make_float2(xb.z, xb.w), tq[mr][kAcc - 1]);
       }
     }
 #pragma unroll
     for (int mr = 0; mr < R; ++mr) {
       const float gs = gsum[mr * kbps + g];
-      acc[mr] = fmaf(sc, fmaf(-128.0f, gs, tq[mr].x + tq[mr].y), fmaf(bi, gs, acc[mr]));
+      const float dot = kAcc == 2 ? (tq[mr][0].x + tq[mr][0].y) + (tq[mr][kAcc - 1].x + tq[mr][kAcc - 1].y)
+                                  : tq[mr][0].x + tq[mr][0].y;
+      acc[mr] = fmaf(sc, fmaf(-128.0f, gs, dot), fmaf(bi, gs, acc[mr]));
     }
   }
   if (landed < nkb && t == 0) {
