@@ -720,14 +720,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 // A CTA owns 128 weight rows (outputs) — exactly one half of a 256-row tile, so
 // its weights for a K block are one contiguous 4608-byte half-chunk — and one
 // K split of the cluster. The split's half-chunks stream through a ring of
-// kGemvRing shared-memory slots: thread 0 bulk-copies the first kGemvRing at
-// once (one mbarrier per slot; the copy engine keeps HBM busy without
-// per-thread loads in flight) and refills a slot as soon as every thread has
-// used it; the threads stage x meanwhile and then take the K blocks in order as
-// they land, one weight row each. The ring keeps the shared memory of a CTA
-// small, so even a 3072 x 18432 weight (215 KB per SM) runs in one wave.
-// Partial sums of the cluster's splits are reduced in CTA rank 0 through
-// distributed shared memory (no scratch, no atomics, fixed order).
+// kGemvRing shared-memory slots owned by a producer warp (lane 0 bulk-copies a
+// K block into a slot, one "full" mbarrier per slot, and refills the slot once
+// each of the four compute warps has arrived on its "empty" mbarrier), so no
+// CTA-wide barrier sits in the K loop. The compute warps stage x meanwhile
+// (group sums of x formed on the way, by shuffles) and then take the K blocks
+// in order as they land, one weight row per thread. The ring keeps the shared
+// memory of a CTA small, so even a 3072 x 18432 weight (215 KB per SM) runs in
+// one wave. Partial sums of the cluster's splits are reduced in CTA rank 0
+// through distributed shared memory (no scratch, no atomics, fixed order).
 // One launch may cover up to kGemvMaxProblems weights that read the same x
 // (the conditioning's modulation heads): the CTAs along x are numbered across
 // the problems, so one launch and one fill/drain serve all of them.
@@ -735,6 +736,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 // affine_qmm_t_float_gs_64_b_4, DirectConditioner.swift:48,183-190); it is
 // staged as f32 either way, so the arithmetic is the same.
 constexpr int kGemvRows = 128;
+constexpr int kGemvThreads = kGemvRows + 32;  // four compute warps + the producer warp
 constexpr int kGemvMaxSplit = 8;   // cluster size along K (portable limit)
 constexpr int kGemvMaxKbps = 48;   // K blocks per CTA
 constexpr int kGemvRing = 4;       // weight slots per CTA
@@ -763,20 +765,22 @@ struct GemvParams {
 __host__ __device__ constexpr size_t gemv_smem_bytes(int R, int kbps) {
   return static_cast<size_t>(kGemvRing) * kHalfBytes                              // weight ring
          + static_cast<size_t>(R) * (kbps * kKB + kbps + kGemvRows) * 4          // x, group sums, partials
-         + 8 + static_cast<size_t>(kGemvRing) * 8;                               // align + barriers
+         + 8 + static_cast<size_t>(kGemvRing) * 16;                              // align + full/empty barriers
 }
 
 template <int R, bool XF32>
-__global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t gsm_raw[];
   const int kbps = p.kb_per_split;
   uint8_t* wsm = gsm_raw;
   float* xs = reinterpret_cast<float*>(gsm_raw + static_cast<size_t>(kGemvRing) * kHalfBytes);
   float* gsum = xs + R * kbps * kKB;
   float* part = gsum + R * kbps;
-  uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(part + R * kGemvRows) + 7) & ~uintptr_t(7));
+  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(part + R * kGemvRows) + 7) & ~uintptr_t(7));
+  uint64_t* empty = full + kGemvRing;
   __shared__ int abort_flag;
   const int t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
   int pi = 0;
 #pragma unroll
   for (int i = 1; i < kGemvMaxProblems; ++i)
@@ -787,152 +791,168 @@ __global__ void __launch_bounds__(kGemvRows) gemv_kernel(const __grid_constant__
   const int kb0 = split * kbps;
   const int kb1 = min(p.k_blocks, kb0 + kbps);
   const int nkb = max(0, kb1 - kb0);
-  const int row = cta * kGemvRows + t;  // weight row (output column)
+  const int row = cta * kGemvRows + t;  // weight row (output column) of a compute thread
   const int nt = cta >> 1, half = cta & 1;
-  const bool active = row < q.n;
-  // 1. Barriers, then the first kGemvRing weight copies of this CTA's K range.
-  auto issue = [&](int g) {  // K block g of the range into slot g % kGemvRing (thread 0)
-    uint64_t* bar = &bars[g % kGemvRing];
-    mbar_arrive_expect_tx(bar, kHalfBytes);
-    bulk_load(wsm + (g % kGemvRing) * kHalfBytes,
-              q.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes, kHalfBytes, bar);
-  };
+  const bool active = t < kGemvRows && row < q.n;
   if (t == 0) {
     abort_flag = 0;
-    for (int s = 0; s < kGemvRing; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kGemvRing; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvRows / 32);
+    }
     fence_barrier_init();
   }
   __syncthreads();
-  int issued = 0;  // copies issued (thread 0)
-  if (t == 0)
-    for (; issued < nkb && issued < kGemvRing; ++issued) issue(issued);
-  // 2. Stage this split's x slice as f32 (16-byte loads: x 16-byte aligned and its row pitch a multiple of 16
-  //    bytes, checked on the host; every load of a thread issued before its stores), then per-group sums.
-  {
-    constexpr int kPerVec = XF32 ? 4 : 8;  // elements per 16-byte load
-    constexpr int kBatch = 4;               // loads in flight per thread before their stores
-    const int per_row = nkb * kKB / kPerVec, nvec = R * per_row;
-#pragma unroll 1
-    for (int j0 = 0; j0 * kGemvRows < nvec; j0 += kBatch) {
-    uint4 xv[kBatch];
+  float acc[R];
 #pragma unroll
-    for (int jj = 0; jj < kBatch; ++jj) {
-      const int j = j0 + jj;
-      const int i = t + j * kGemvRows;
-      xv[jj] = make_uint4(0, 0, 0, 0);
-      if (i < nvec) {
-        const int mr = i / per_row, c = i % per_row;
-        if (mr < p.m) {
-          if (XF32)
-            xv[jj] = __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.x) +
-                                                          static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
-          else
-            xv[jj] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
-                                                          static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
-        }
+  for (int mr = 0; mr < R; ++mr) acc[mr] = 0.f;
+  if (warp == kGemvRows / 32) {
+    // 1. Producer: K block g of the range into slot g % kGemvRing once the slot's previous block is used.
+    if (lane == 0) {
+      int issued = 0;
+      for (int g = 0; g < nkb; ++g) {
+        const int s = g % kGemvRing;
+        if (g >= kGemvRing &&
+            !mbar_wait(&empty[s], ((g / kGemvRing) - 1) & 1, &abort_flag, p.status, kDevTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(&full[s], kHalfBytes);
+        bulk_load(wsm + s * kHalfBytes, q.tiles + chunk_offset(nt, kb0 + g, p.k_blocks) + half * kHalfBytes,
+                  kHalfBytes, &full[s]);
+        issued = g + 1;
       }
-    }
-#pragma unroll
-    for (int jj = 0; jj < kBatch; ++jj) {
-      const int i = t + (j0 + jj) * kGemvRows;
-      if (i < nvec) {
-        const int mr = i / per_row, c = i % per_row;
-        float* d = xs + mr * kbps * kKB + c * kPerVec;
-        const uint32_t u[4] = {xv[jj].x, xv[jj].y, xv[jj].z, xv[jj].w};
-        if (XF32) {
-          *reinterpret_cast<float4*>(d) =
-              make_float4(__uint_as_float(u[0]), __uint_as_float(u[1]), __uint_as_float(u[2]), __uint_as_float(u[3]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            d[2 * e] = bf16lo_to_f32(u[e]);
-            d[2 * e + 1] = bf16hi_to_f32(u[e]);
+      if (issued < nkb) {
+        // Aborting: the copies still in flight (at most the last kGemvRing issued) land before the CTA exits.
+        for (int g = max(0, issued - kGemvRing); g < issued; ++g) {
+          const uint32_t a = smem_u32(&full[g % kGemvRing]);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(a, (g / kGemvRing) & 1) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
           }
         }
       }
     }
+    __syncwarp();
+  } else {
+    // 2. Stage this split's x slice as f32 (16-byte loads: x 16-byte aligned and its row pitch a multiple of 16
+    //    bytes, checked on the host; every load of a thread issued before its stores) and the per-group sums:
+    //    the 16-byte vectors of one 64-element group sit in kVpg consecutive lanes, summed by shuffles.
+    {
+      constexpr int kPerVec = XF32 ? 4 : 8;  // elements per 16-byte load
+      constexpr int kVpg = kKB / kPerVec;     // vectors per group
+      constexpr int kBatch = 4;               // loads in flight per thread before their stores
+      const int per_row = nkb * kKB / kPerVec, nvec = R * per_row;
+#pragma unroll 1
+      for (int j0 = 0; j0 * kGemvRows < nvec; j0 += kBatch) {
+        uint4 xv[kBatch];
+#pragma unroll
+        for (int jj = 0; jj < kBatch; ++jj) {
+          const int i = t + (j0 + jj) * kGemvRows;
+          xv[jj] = make_uint4(0, 0, 0, 0);
+          if (i < nvec) {
+            const int mr = i / per_row, c = i % per_row;
+            if (mr < p.m) {
+              if (XF32)
+                xv[jj] = __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.x) +
+                                                              static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
+              else
+                xv[jj] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) +
+                                                              static_cast<int64_t>(mr) * p.ldx + kb0 * kKB) + c);
+            }
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < kBatch; ++jj) {
+          const int i = t + (j0 + jj) * kGemvRows;
+          float vs = 0.f;
+          if (i < nvec) {
+            const int mr = i / per_row, c = i % per_row;
+            float* d = xs + mr * kbps * kKB + c * kPerVec;
+            const uint32_t u[4] = {xv[jj].x, xv[jj].y, xv[jj].z, xv[jj].w};
+            if (XF32) {
+              const float4 f = make_float4(__uint_as_float(u[0]), __uint_as_float(u[1]), __uint_as_float(u[2]),
+                                           __uint_as_float(u[3]));
+              *reinterpret_cast<float4*>(d) = f;
+              vs = (f.x + f.y) + (f.z + f.w);
+            } else {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                f[2 * e] = bf16lo_to_f32(u[e]);
+                f[2 * e + 1] = bf16hi_to_f32(u[e]);
+              }
+              *reinterpret_cast<float4*>(d) = make_float4(f[0], f[1], f[2], f[3]);
+              *reinterpret_cast<float4*>(d + 4) = make_float4(f[4], f[5], f[6], f[7]);
+              vs = ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
+            }
+          }
+#pragma unroll
+          for (int o = 1; o < kVpg; o <<= 1) vs += __shfl_xor_sync(0xffffffffu, vs, o);
+          if (i < nvec && i % kVpg == 0) {
+            const int mr = i / per_row, c = i % per_row;
+            gsum[mr * kbps + c / kVpg] = vs;
+          }
+        }
+      }
     }
-  }
-  __syncthreads();
-  {
-    const int warp = t >> 5, lane = t & 31;
-    for (int i = warp; i < R * nkb; i += kGemvRows / 32) {
-      const int mr = i / nkb, g = i % nkb;
-      const float* xg = xs + mr * kbps * kKB + g * kKB;
-      float s = xg[lane] + xg[lane + 32];
+    asm volatile("bar.sync 1, %0;" ::"r"(kGemvRows) : "memory");  // the four compute warps
+    // 3. Dot products per group as its weights land: y_m += scale * sum_k(x_mk * q_k) +
+    //    bias * sum_k(x_mk), the unrounded dequantized weights. The codes enter as exact f32 (128 + q)
+    //    and the offset is removed once per group (sum x (128 + q) - 128 sum x; products exact, f32 sums).
+    for (int g = 0; g < nkb; ++g) {
+      const int s = g % kGemvRing;
+      if (!mbar_wait_warp(&full[s], (g / kGemvRing) & 1, &abort_flag, p.status, kDevTimeoutTma)) break;
+      uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+      float sc = 0.f, bi = 0.f;
+      if (active) {
+        const uint8_t* hb = wsm + s * kHalfBytes;
+        w0 = *reinterpret_cast<const uint4*>(hb + t * 32);
+        w1 = *reinterpret_cast<const uint4*>(hb + t * 32 + 16);
+        sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4096 + t * 2));
+        bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4352 + t * 2));
+      }
+      // The warp's reads of the slot are done: release it to the producer.
+      __syncwarp();
+      if (lane == 0) mbar_arrive_addr(smem_u32(&empty[s]));
+      if (!active) continue;
+      const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      // Two accumulator pairs per row (codes 0,1,4,5 and 2,3,6,7 of each word) at R = 1 for a shorter
+      // dependency chain; one pair per row otherwise.
+      constexpr int kAcc = R == 1 ? 2 : 1;
+      float2 tq[R][kAcc];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) gsum[mr * kbps + g] = s;
-    }
-  }
-  __syncthreads();
-  // 3. Dot products per group as its weights land: y_m += scale * sum_k(x_mk * q_k) +
-  //    bias * sum_k(x_mk), the unrounded dequantized weights. The codes enter as exact f32 (128 + q)
-  //    and the offset is removed once per group (sum x (128 + q) - 128 sum x; products exact, f32 sums).
-  float acc[R];
+      for (int mr = 0; mr < R; ++mr)
 #pragma unroll
-  for (int mr = 0; mr < R; ++mr) acc[mr] = 0.f;
-  int landed = 0;
-  for (int g = 0; g < nkb; ++g) {
-    const bool got = mbar_wait(&bars[g % kGemvRing], (g / kGemvRing) & 1, &abort_flag, p.status, kDevTimeoutTma);
-    // Uniform across the CTA: block g has landed and every thread is done with block g - 1.
-    if (!__syncthreads_and(got)) break;
-    landed = g + 1;
-    if (t == 0 && g >= 1 && issued < nkb) issue(issued++);  // refill the slot block g - 1 used
-    if (!active) continue;
-    const uint8_t* hb = wsm + (g % kGemvRing) * kHalfBytes;
-    const uint4 w0 = *reinterpret_cast<const uint4*>(hb + t * 32);
-    const uint4 w1 = *reinterpret_cast<const uint4*>(hb + t * 32 + 16);
-    const float sc = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4096 + t * 2));
-    const float bi = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(hb + 4352 + t * 2));
-    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    // Two accumulator pairs per row (codes 0,1,4,5 and 2,3,6,7 of each word) at R = 1 for a shorter
-    // dependency chain; one pair per row otherwise.
-    constexpr int kAcc = R == 1 ? 2 : 1;
-    float2 tq[R][kAcc];
+        for (int a = 0; a < kAcc; ++a) tq[mr][a] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int mr = 0; mr < R; ++mr)
+      for (int c = 0; c < 8; ++c) {
+        // Codes 2j / 2j+1 of a permuted word sit at bits 4j / 16+4j, so the low nibbles of its bytes are codes
+        // 0, 4, 1, 5 and the high nibbles codes 2, 6, 3, 7; one byte permute per code makes the f32 128 + q.
+        const uint32_t lo = ws[c] & 0x0F0F0F0Fu, hi = (ws[c] >> 4) & 0x0F0F0F0Fu;
+        const float2 q01 = make_float2(code_f32_128(lo, 0), code_f32_128(lo, 2));
+        const float2 q23 = make_float2(code_f32_128(hi, 0), code_f32_128(hi, 2));
+        const float2 q45 = make_float2(code_f32_128(lo, 1), code_f32_128(lo, 3));
+        const float2 q67 = make_float2(code_f32_128(hi, 1), code_f32_128(hi, 3));
+        const int kk = g * kKB + c * 8;  // codes kk .. kk+7
 #pragma unroll
-      for (int a = 0; a < kAcc; ++a) tq[mr][a] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      // Codes 2j / 2j+1 of a permuted word sit at bits 4j / 16+4j, so the low nibbles of its bytes are codes
-      // 0, 4, 1, 5 and the high nibbles codes 2, 6, 3, 7; one byte permute per code makes the f32 128 + q.
-      const uint32_t lo = ws[c] & 0x0F0F0F0Fu, hi = (ws[c] >> 4) & 0x0F0F0F0Fu;
-      const float2 q01 = make_float2(code_f32_128(lo, 0), code_f32_128(lo, 2));
-      const float2 q23 = make_float2(code_f32_128(hi, 0), code_f32_128(hi, 2));
-      const float2 q45 = make_float2(code_f32_128(lo, 1), code_f32_128(lo, 3));
-      const float2 q67 = make_float2(code_f32_128(hi, 1), code_f32_128(hi, 3));
-      const int kk = g * kKB + c * 8;  // codes kk .. kk+7
+        for (int mr = 0; mr < R; ++mr) {
+          const float4 xa = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
+          const float4 xb = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk + 4);
+          tq[mr][0] = ffma2(q01, make_float2(xa.x, xa.y), tq[mr][0]);
+          tq[mr][kAcc - 1] = ffma2(q23, make_float2(xa.z, xa.w), tq[mr][kAcc - 1]);
+          tq[mr][0] = ffma2(q45, make_float2(xb.x, xb.y), tq[mr][0]);
+          tq[mr][kAcc - 1] = ffma2(q67, make_float2(xb.z, xb.w), tq[mr][kAcc - 1]);
+        }
+      }
 #pragma unroll
       for (int mr = 0; mr < R; ++mr) {
-        const float4 xa = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk);
-        const float4 xb = *reinterpret_cast<const float4*>(xs + mr * kbps * kKB + kk + 4);
-        tq[mr][0] = ffma2(q01, make_float2(xa.x, xa.y), tq[mr][0]);
-        tq[mr][kAcc - 1] = ffma2(q23, make_float2(xa.z, xa.w), tq[mr][kAcc - 1]);
-        tq[mr][0] = ffma2(q45, make_float2(xb.x, xb.y), tq[mr][0]);
-        tq[mr][kAcc - 1] = ffma2(q67, make_float2(xb.z, xb.w), tq[mr][kAcc - 1]);
+        const float gs = gsum[mr * kbps + g];
+        const float dot = kAcc == 2 ? (tq[mr][0].x + tq[mr][0].y) + (tq[mr][kAcc - 1].x + tq[mr][kAcc - 1].y)
+                                    : tq[mr][0].x + tq[mr][0].y;
+        acc[mr] = fmaf(sc, fmaf(-128.0f, gs, dot), fmaf(bi, gs, acc[mr]));
       }
     }
 #pragma unroll
-    for (int mr = 0; mr < R; ++mr) {
-      const float gs = gsum[mr * kbps + g];
-      const float dot = kAcc == 2 ? (tq[mr][0].x + tq[mr][0].y) + (tq[mr][kAcc - 1].x + tq[mr][kAcc - 1].y)
-                                  : tq[mr][0].x + tq[mr][0].y;
-      acc[mr] = fmaf(sc, fmaf(-128.0f, gs, dot), fmaf(bi, gs, acc[mr]));
-    }
+    for (int mr = 0; mr < R; ++mr) part[mr * kGemvRows + t] = acc[mr];
   }
-  if (landed < nkb && t == 0) {
-    // Aborting: let the copies still in flight land before the CTA can exit.
-    for (int g = landed; g < issued; ++g) {
-      const uint32_t a = smem_u32(&bars[g % kGemvRing]);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(a, (g / kGemvRing) & 1) && globaltimer_ns() - t0 < kWaitTimeoutNs) {
-      }
-    }
-  }
-#pragma unroll
-  for (int mr = 0; mr < R; ++mr) part[mr * kGemvRows + t] = acc[mr];
   // 4. Reduce the K splits of this cluster in CTA rank 0 through distributed shared memory.
   cluster_sync_all();
   if (cluster_ctarank() == 0 && active) {
@@ -1005,6 +1025,14 @@ int launch_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
   // fewest waves of the SMs at the residency their shared memory allows, then the largest (more copies in
   // flight per output row).
   auto smem_for = [&](int kb) { return qmm::gemv_smem_bytes(R, kb); };
+  auto kern = qmm::gemv_kernel<R, XF32>;
+  // CTAs per SM allowed by threads and registers (65536 per SM, allocated per warp in units of 256).
+  static const int reg_limit = [&] {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs <= 0) return 1;
+    const int per_warp = (fa.numRegs * 32 + 255) / 256 * 256;
+    return std::max(1, 65536 / (per_warp * (qmm::kGemvThreads / 32)));
+  }();
   constexpr size_t kMaxSmem = 200 * 1024;
   constexpr size_t kSmPerSm = 228 * 1024;  // shared memory of one SM
   const int min_split = (w0->k_blocks + qmm::kGemvMaxKbps - 1) / qmm::kGemvMaxKbps;
@@ -1016,7 +1044,8 @@ int launch_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
   for (int sp = min_split; sp <= std::min(qmm::kGemvMaxSplit, w0->k_blocks); ++sp) {
     const int kb = (w0->k_blocks + sp - 1) / sp;
     if ((w0->k_blocks + kb - 1) / kb != sp || smem_for(kb) > kMaxSmem) continue;  // an empty split, or too big
-    const int64_t per_sm = std::min<int64_t>(16, static_cast<int64_t>(kSmPerSm / (smem_for(kb) + 1024)));
+    const int64_t per_sm = std::min<int64_t>(std::min({16, 2048 / qmm::kGemvThreads, reg_limit}),
+                                             static_cast<int64_t>(kSmPerSm / (smem_for(kb) + 1024)));
     const int64_t slots = per_sm * ctx->sm_count;
     const int64_t waves = (static_cast<int64_t>(n_ctas) * sp + slots - 1) / slots;
     if (split == 0 || waves <= best_waves) {
@@ -1027,11 +1056,10 @@ int launch_gemv(aex_ctx* ctx, const QmmJob* jobs, int n, cudaStream_t s) {
   if (split == 0) return set_error(ctx, AEX_ERR_UNSUPPORTED, "qmm gemv: k=%d too large for %d rows", w0->k, R);
   const int kbps = (w0->k_blocks + split - 1) / split;
   p.kb_per_split = kbps;
-  auto kern = qmm::gemv_kernel<R, XF32>;
   AEX_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxSmem)));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(n_ctas, split, 1);
-  cfg.blockDim = dim3(qmm::kGemvRows, 1, 1);
+  cfg.blockDim = dim3(qmm::kGemvThreads, 1, 1);
   cfg.dynamicSmemBytes = smem_for(kbps);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
