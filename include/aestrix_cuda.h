@@ -318,9 +318,10 @@ int aex_comm_abort(aex_comm* comm);
 int aex_ring_attention(aex_ctx* ctx, aex_comm* comm, const aex_attention_args* args, aex_stream stream);
 /* The exchange schedule aex_ring_attention and the sequence-parallel engine take
  * for `world` shards of `seq` tokens x `heads` heads: 0 ring, 1 all-gather,
- * 2 overlap (pairwise exchange overlapped with per-shard attention; the
- * default for world > 1 while the gathered K/V fit in 8 GiB), -1 bad
- * arguments. AEX_SP_SCHEDULE=overlap|gather|ring overrides. */
+ * 2 overlap (pairwise exchange overlapped with per-shard attention). While
+ * the gathered K/V fit in 8 GiB the default is overlap at world 2 and
+ * all-gather otherwise, else ring; -1 bad arguments.
+ * AEX_SP_SCHEDULE=overlap|gather|ring overrides. */
 int aex_sp_schedule(int world, int seq, int heads);
 
 /* One step of the overlap schedule's plan (host logic, no GPU needed). */

@@ -198,12 +198,12 @@ _SCHEDULE_PROBE = (
     "L.aex_sp_schedule(1, 2112, 24), L.aex_sp_schedule(0, 2112, 24), L.aex_sp_schedule(2, 0, 24))")
 
 
-@pytest.mark.parametrize("env,want", [(None, "2 2 0 1 -1 -1"), ("ring", "0 0 0 0 -1 -1"), ("gather", "1 1 1 1 -1 -1"),
+@pytest.mark.parametrize("env,want", [(None, "1 2 0 1 -1 -1"), ("ring", "0 0 0 0 -1 -1"), ("gather", "1 1 1 1 -1 -1"),
                                       ("overlap", "2 2 2 2 -1 -1")])
 def test_sp_schedule_choice(env, want):
-    """Overlap for more than one rank while the gathered K/V (2 * world * seq * heads * 256 bytes) fit in 8 GiB,
-    all-gather for one rank, ring beyond; AEX_SP_SCHEDULE overrides. Each case in a fresh process: the override
-    is read once."""
+    """While the gathered K/V (2 * world * seq * heads * 256 bytes) fit in 8 GiB: overlap at two ranks,
+    all-gather at one or more than two; ring beyond; AEX_SP_SCHEDULE overrides. Each case in a fresh process:
+    the override is read once."""
     e = {k: v for k, v in os.environ.items() if k != "AEX_SP_SCHEDULE"}
     if env:
         e["AEX_SP_SCHEDULE"] = env
