@@ -87,6 +87,39 @@ def test_joint_attention_baseline_configs(cuda_ctx, grid, seed):
     _compare(out, ref, rows)
 
 
+# --- few heads per call (each GPU's call in the head-sharded 1024^2 config): keys split into ranges -------------
+@pytest.mark.parametrize("heads", [3, 6, 12])
+def test_few_heads_split_keys(cuda_ctx, heads):
+    """A 1024^2 call on a slice of 24 / N heads (strided views, as each GPU of the head-sharded config makes it)
+    underfills the SMs, so the allocating entry point splits its keys into ranges merged by log2-sum-exp
+    (aex_sp_key_ranges reports how many). Checked against the oracle on sampled rows and against the same heads
+    of the 24-head call, which runs unsplit."""
+    l_txt, grid = 512, 64
+    s = l_txt + grid * grid
+    assert _lib.lib().aex_sp_key_ranges(1, s, heads, cuda_ctx.sm_count) > 1
+    assert _lib.lib().aex_sp_key_ranges(1, s, 24, cuda_ctx.sm_count) == 1
+    q, k, v = _inputs(1, s, 24, 21)
+    wq, wk = _norm_weights(121)
+    cos, sin = _rope(l_txt, grid, grid)
+    dev = torch.device("cuda")
+    qd, kd, vd = (t.to(dev) for t in (q, k, v))
+    args = (wq.to(dev), wk.to(dev), 1e-6, torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev))
+    h0 = 24 - heads
+    out = attention.joint_attention(qd[:, :, h0:], kd[:, :, h0:], vd[:, :, h0:], *args)
+    full = attention.joint_attention(qd, kd, vd, *args)
+    torch.cuda.synchronize()
+    a, b = out.float(), full[:, :, h0:].float()
+    rel = float((a - b).norm() / b.norm())
+    assert rel <= 5e-3, f"split vs unsplit rel-L2 {rel:.3e}"
+    rows = np.r_[0:32, l_txt - 16:l_txt + 16, s - 32:s]
+    ref = np.full((1, s, heads, 128), np.nan, np.float32)
+    qs, ks, vs = (t[:, :, h0:].float().contiguous().numpy() for t in (q, k, v))
+    for lo, hi in ((0, 32), (l_txt - 16, l_txt + 16), (s - 32, s)):
+        part = O.joint_attention(qs, ks, vs, wq.numpy(), wk.numpy(), 1e-6, cos, sin, q_begin=lo, q_end=hi)
+        ref[:, lo:hi] = part[:, lo:hi]
+    _compare(out, ref, rows)
+
+
 # --- i2i (image-to-image conditioning): text 512 + target 64x64 + reference 64x64, J = 8,704 -----------------------
 def test_joint_attention_i2i_8704(cuda_ctx):
     """Image-to-image joint sequence: the reference image's tokens carry ids (10, h, w, 0)
