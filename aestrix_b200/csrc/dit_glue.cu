@@ -103,6 +103,79 @@ __global__ void __launch_bounds__(kRowThreads) ln_mod_kernel(const float* __rest
 }
 
 
+// The same LayerNorm + modulation with the row held in registers (C <= NV * 4 * kRowThreads): one read of
+// the row from memory, the sum and the magnitude reduced together, then the centered variance from registers.
+// Sums are taken in a different order than ln_mod_kernel's (each thread's four-element groups first).
+__device__ __forceinline__ float2 block_sum_max(float2 v, float2* red2) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+    v.y = fmaxf(v.y, __shfl_xor_sync(0xffffffffu, v.y, o));
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red2[w] = v;
+  __syncthreads();
+  float2 t = l < (blockDim.x >> 5) ? red2[l] : make_float2(0.f, 0.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    t.x += __shfl_xor_sync(0xffffffffu, t.x, o);
+    t.y = fmaxf(t.y, __shfl_xor_sync(0xffffffffu, t.y, o));
+  }
+  return t;  // every warp reduces the partials itself: no second barrier
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kRowThreads) ln_mod_reg_kernel(const float* __restrict__ x, int64_t ldx, int C,
+                                                                 const float* __restrict__ scale,
+                                                                 const float* __restrict__ shift, float eps,
+                                                                 __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  __shared__ float2 red2[2][32];
+  const float* xr = x + static_cast<int64_t>(blockIdx.x) * ldx;
+  float4 v[NV];
+  float s = 0.f, amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = (threadIdx.x + k * kRowThreads) * 4;
+    v[k] = i < C ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+  }
+  const float2 sm = block_sum_max(make_float2(s, amax), red2[0]);
+  const float mean = sm.x / C;
+  // 2^-e with 2^e the power of two at or below amax, when amax > 2^48 (else 1)
+  const float sc = (sm.y > 281474976710656.0f && sm.y <= 3.4028235e38f)
+                       ? __uint_as_float((254u - ((__float_as_uint(sm.y) >> 23) & 0xFFu)) << 23)
+                       : 1.0f;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = (threadIdx.x + k * kRowThreads) * 4;
+    if (i < C) {
+      const float a = (v[k].x - mean) * sc, b = (v[k].y - mean) * sc, c = (v[k].z - mean) * sc,
+                  d = (v[k].w - mean) * sc;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+  const float inv = rsqrtf(block_sum_max(make_float2(q, 0.f), red2[1]).x / C + eps * sc * sc) * sc;
+  __nv_bfloat16* yr = y + static_cast<int64_t>(blockIdx.x) * ldy;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = (threadIdx.x + k * kRowThreads) * 4;
+    if (i < C) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(scale + i));
+      const float4 h = __ldg(reinterpret_cast<const float4*>(shift + i));
+      const float o0 = fmaf(1.f + g.x, (v[k].x - mean) * inv, h.x);
+      const float o1 = fmaf(1.f + g.y, (v[k].y - mean) * inv, h.y);
+      const float o2 = fmaf(1.f + g.z, (v[k].z - mean) * inv, h.z);
+      const float o3 = fmaf(1.f + g.w, (v[k].w - mean) * inv, h.w);
+      *reinterpret_cast<uint2*>(yr + i) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+    }
+  }
+}
+
 __global__ void gate_add_kernel(float* __restrict__ x, int64_t ldx, int rows, int C, const float* __restrict__ gate,
                                 const uint16_t* __restrict__ v, int64_t ldv, float scale) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -174,7 +247,18 @@ int ln_mod(aex_ctx* ctx, const float* x, int64_t ldx, int rows, int C, const flo
            float eps, void* y, int64_t ldy, cudaStream_t s) {
   if (rows <= 0) return AEX_OK;
   if (C % 4 || ldx % 4 || ldy % 4) return set_error(ctx, AEX_ERR_INVALID_ARG, "ln_mod: C and pitches must be multiples of 4");
-  ln_mod_kernel<<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, static_cast<__nv_bfloat16*>(y), ldy);
+  __nv_bfloat16* yb = static_cast<__nv_bfloat16*>(y);
+  const int nv = (C + 4 * kRowThreads - 1) / (4 * kRowThreads);  // float4 per thread to hold the row
+  if (nv <= 1)
+    ln_mod_reg_kernel<1><<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, yb, ldy);
+  else if (nv <= 2)
+    ln_mod_reg_kernel<2><<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, yb, ldy);
+  else if (nv <= 3)
+    ln_mod_reg_kernel<3><<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, yb, ldy);
+  else if (nv <= 4)
+    ln_mod_reg_kernel<4><<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, yb, ldy);
+  else
+    ln_mod_kernel<<<rows, kRowThreads, 0, s>>>(x, ldx, C, scale, shift, eps, yb, ldy);
   return check_launch(ctx, "ln_mod_kernel");
 }
 
