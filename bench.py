@@ -320,7 +320,7 @@ def run_reference(args):
 def measure_qmm(ctx, dev, iters=60):
     """4-bit affine linears 3072 -> 9216 (QKV) and 3072 -> 18432 (SwiGLU) at
     M in {4608, 512, 1}. Weights rotate over enough device copies to exceed L2 (> 160 MB), so every
-    call streams its weight from HBM. The timed calls (whole rounds over the weight copies, >= 48 per
+    call streams its weight from HBM. The timed calls (whole passes over the weight copies, >= 48 per
     graph) are replayed from a CUDA graph, so the device time of back-to-back calls is measured without
     the host's per-call cost (which exceeds a 10 us GEMV). TFLOP/s = 2*M*N*K / time; GB/s = algorithmic bytes
     (N*K/2 packed + N*K/64*4 bf16 scale+bias + 2*M*K x + 2*M*N y) / time."""
@@ -344,7 +344,7 @@ def measure_qmm(ctx, dev, iters=60):
                 for i in range(3):
                     ws[i % copies](x, out=y, stream=gs)
             torch.cuda.synchronize()
-            # One graph holds at least 48 calls (whole rounds over the copies), so the gap between graph
+            # One graph holds at least 48 calls (whole passes over the copies), so the gap between graph
             # replays is spread over many calls.
             calls = copies * max(1, math.ceil(48 / copies))
             graph = torch.cuda.CUDAGraph()
