@@ -74,7 +74,8 @@ def test_dequant_golden_and_double_rounding(cuda_ctx):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 300, 640), (2, 512, 256), (5, 1000, 192), (16, 768, 3072),
-                                   (17, 300, 640), (130, 520, 256), (300, 256, 1024), (1, 256, 9216)])
+                                   (17, 300, 640), (130, 520, 256), (300, 256, 1024), (1, 256, 9216),
+                                   (3, 1300, 1536), (8, 640, 12288), (1, 128, 24576)])
 def test_qmm_vs_oracle(cuda_ctx, m, n, k):
     packed, scales, biases = qmm.synthetic_weight(n, k, seed=7 * m + n)
     g = torch.Generator().manual_seed(m * 1000 + k)
