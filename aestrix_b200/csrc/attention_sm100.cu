@@ -18,7 +18,7 @@
 //  * attn_fwd_kernel — one CTA per (256 query rows, head, batch), 12 warps:
 //      warps 0-3   softmax warpgroup of query tile 0 (one query row per thread)
 //      warps 4-7   softmax warpgroup of query tile 1
-//      warp 8      TMA producer (Q tiles once, K/V blocks through a 4-slot ring)
+//      warp 8      TMA producer (Q tiles once, K/V blocks through a 5-slot ring)
 //      warp 9      UMMA issuer (one thread)
 //      warps 10-11 idle (complete the control warpgroup for setmaxnreg)
 //    Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,384),
@@ -46,7 +46,7 @@ constexpr int kD = 128;
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // keys per block
 constexpr int kTiles = 2;
-constexpr int kStages = 4;
+constexpr int kStages = 5;  // K/V ring slots: 2 x 32 KB Q + 5 x 32 KB = 224 KB of the 227 KB a CTA may use
 constexpr int kTileBytes = kBM * kD * 2;  // 32 KB, two 16 KB swizzle regions of 64 columns
 constexpr int kRegionBytes = kTileBytes / 2;
 // 12 warps = 3 warpgroups: two softmax warpgroups (one query row per thread)
